@@ -1,0 +1,562 @@
+/*
+ * vk_oracle.c -- CPU restatement of the vestra-kernels reference arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY (the parity checker; never on the product path).
+ *
+ * Compile with -ffp-contract=off: Rust never contracts a*b+c into an FMA, so
+ * every multiply-add below is two rounded operations unless the reference
+ * itself uses an FMA intrinsic, in which case fmaf() is called explicitly.
+ * Rust's `iter().sum::<f32>()` is a left fold that starts from -0.0; the
+ * folds below start from -0.0f for the same reason.
+ */
+#include "vk_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+void vko_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
+/* ------------------------------------------------------------------ */
+/* half / bfloat16 conversions                                         */
+/* ------------------------------------------------------------------ */
+
+static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* IEEE-754 binary32 -> binary16, round to nearest, ties to even (the rule
+ * half::f16::from_f32 implements, in hardware through F16C or in software). */
+uint16_t vko_f16_from_f32(float x) {
+  uint32_t u = f2u(x);
+  uint16_t sign = (uint16_t)((u >> 16) & 0x8000u);
+  uint32_t exp = (u >> 23) & 0xffu;
+  uint32_t man = u & 0x7fffffu;
+  if (exp == 0xffu) { /* inf / nan */
+    if (man == 0) return sign | 0x7c00u;
+    return sign | 0x7e00u | (uint16_t)(man >> 13);
+  }
+  int e = (int)exp - 127 + 15;
+  if (e >= 0x1f) return sign | 0x7c00u; /* overflow -> inf */
+  if (e <= 0) {
+    /* subnormal half (or zero) */
+    if (e < -10) return sign; /* rounds to zero */
+    uint32_t m = man | 0x800000u;     /* implicit bit */
+    int shift = 14 - e;               /* 24-bit mantissa -> 10-bit field */
+    uint32_t half_m = m >> shift;
+    uint32_t rem = m & ((1u << shift) - 1u);
+    uint32_t halfway = 1u << (shift - 1);
+    if (rem > halfway || (rem == halfway && (half_m & 1u))) half_m++;
+    return sign | (uint16_t)half_m;
+  }
+  uint32_t half_m = man >> 13;
+  uint32_t rem = man & 0x1fffu;
+  uint16_t h = sign | (uint16_t)((uint32_t)e << 10) | (uint16_t)half_m;
+  if (rem > 0x1000u || (rem == 0x1000u && (half_m & 1u))) h++; /* carries into exp ok */
+  return h;
+}
+
+float vko_f16_to_f32(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1fu;
+  uint32_t man = h & 0x3ffu;
+  if (exp == 0) {
+    if (man == 0) return u2f(sign);
+    /* subnormal: value = man * 2^-24, exact in f32 */
+    float v = (float)man * 5.9604644775390625e-8f;
+    return sign ? -v : v;
+  }
+  if (exp == 0x1f) return u2f(sign | 0x7f800000u | (man << 13));
+  return u2f(sign | ((exp - 15 + 127) << 23) | (man << 13));
+}
+
+float vko_round_bf16(float x) {
+  uint32_t u = f2u(x);
+  if ((u & 0x7f800000u) == 0x7f800000u) { /* inf / nan */
+    if (u & 0x7fffffu) return u2f((u | 0x400000u) & 0xffff0000u);
+    return x;
+  }
+  uint32_t lsb = (u >> 16) & 1u;
+  u += 0x7fffu + lsb;
+  return u2f(u & 0xffff0000u);
+}
+
+/* ------------------------------------------------------------------ */
+/* src/scalar.rs                                                       */
+/* ------------------------------------------------------------------ */
+
+/* src/scalar.rs:3-18: c[i,j] = 0; for p: c[i,j] += a[i,p] * b[p,j].  The
+ * rows are independent and each element keeps its ascending-p order. */
+void vko_gemm_f32(size_t m, size_t n, size_t k, const float* a, const float* b, float* c) {
+#pragma omp parallel for schedule(static)
+  for (size_t i = 0; i < m; ++i) {
+    float* ci = c + i * n;
+    for (size_t j = 0; j < n; ++j) ci[j] = 0.0f;
+    for (size_t p = 0; p < k; ++p) {
+      const float aip = a[i * k + p];
+      const float* bp = b + p * n;
+      for (size_t j = 0; j < n; ++j) ci[j] += aip * bp[j];
+    }
+  }
+}
+
+/* src/scalar.rs:25-56: acc += d_a * d_b * isum over ascending blocks. */
+void vko_gemm_q8_0(size_t m, size_t n, size_t k, const vko_block_q8_0* a_q,
+                   const vko_block_q8_0* b_q, float* c) {
+  const size_t nb = k / VKO_QK8_0;
+#pragma omp parallel for schedule(static)
+  for (size_t i = 0; i < m; ++i) {
+    const vko_block_q8_0* ar = a_q + i * nb;
+    for (size_t j = 0; j < n; ++j) {
+      const vko_block_q8_0* br = b_q + j * nb;
+      float acc = 0.0f;
+      for (size_t bi = 0; bi < nb; ++bi) {
+        int32_t isum = 0;
+        for (int l = 0; l < VKO_QK8_0; ++l) isum += (int32_t)ar[bi].qs[l] * (int32_t)br[bi].qs[l];
+        acc += vko_f16_to_f32(ar[bi].d) * vko_f16_to_f32(br[bi].d) * (float)isum;
+      }
+      c[i * n + j] = acc;
+    }
+  }
+}
+
+void vko_q8_0_block_dots(size_t m, size_t n, size_t k, const vko_block_q8_0* a_q,
+                         const vko_block_q8_0* b_q, int32_t* out) {
+  const size_t nb = k / VKO_QK8_0;
+#pragma omp parallel for schedule(static)
+  for (size_t i = 0; i < m; ++i)
+    for (size_t j = 0; j < n; ++j)
+      for (size_t bi = 0; bi < nb; ++bi) {
+        int32_t isum = 0;
+        for (int l = 0; l < VKO_QK8_0; ++l)
+          isum += (int32_t)a_q[i * nb + bi].qs[l] * (int32_t)b_q[j * nb + bi].qs[l];
+        out[(i * n + j) * nb + bi] = isum;
+      }
+}
+
+/* src/lib.rs:42-50 */
+void vko_dequantize_q8_0(const vko_block_q8_0* blocks, size_t nblocks, float* out) {
+  for (size_t b = 0; b < nblocks; ++b) {
+    const float scale = vko_f16_to_f32(blocks[b].d);
+    for (int l = 0; l < VKO_QK8_0; ++l) out[b * VKO_QK8_0 + l] = scale * (float)blocks[b].qs[l];
+  }
+}
+
+/* Rust f32::max: returns the non-NaN operand when one is NaN. */
+static inline float rs_max(float a, float b) { return fmaxf(a, b); }
+
+/* src/q8_0_dot.rs:27-46.  amax folds from 0 with f32::max; d = amax / 127;
+ * inv_d is computed from the f32 d (not the rounded f16); round() is
+ * half-away-from-zero (C roundf); clamp to [-127, 127] then truncate to i8. */
+void vko_quantize_row_q8_0(const float* x, size_t nblocks, vko_block_q8_0* out) {
+  for (size_t bi = 0; bi < nblocks; ++bi) {
+    const float* src = x + bi * VKO_QK8_0;
+    float amax = 0.0f;
+    for (int j = 0; j < VKO_QK8_0; ++j) amax = rs_max(amax, fabsf(src[j]));
+    const float d = amax / 127.0f;
+    const float inv_d = (d != 0.0f) ? 1.0f / d : 0.0f;
+    out[bi].d = vko_f16_from_f32(d);
+    for (int j = 0; j < VKO_QK8_0; ++j) {
+      float q = roundf(src[j] * inv_d);
+      if (q < -127.0f) q = -127.0f;
+      if (q > 127.0f) q = 127.0f;
+      out[bi].qs[j] = (int8_t)q;
+    }
+  }
+}
+
+/* src/scalar.rs:58-63 */
+void vko_add(float* dst, const float* src, size_t n) {
+  for (size_t i = 0; i < n; ++i) dst[i] += src[i];
+}
+
+/* src/scalar.rs:65-81 */
+void vko_add_bias_rows(float* x, size_t rows, size_t cols, const float* bias) {
+#pragma omp parallel for schedule(static)
+  for (size_t r = 0; r < rows; ++r)
+    for (size_t c = 0; c < cols; ++c) x[r * cols + c] += bias[c];
+}
+
+/* src/scalar.rs:97-114 */
+static void layernorm_row(float* row, size_t cols, const float* gamma, const float* beta,
+                          float eps) {
+  float s = -0.0f;
+  for (size_t c = 0; c < cols; ++c) s += row[c];
+  const float mean = s / (float)cols;
+  float v = -0.0f;
+  for (size_t c = 0; c < cols; ++c) {
+    const float d = row[c] - mean;
+    v += d * d;
+  }
+  const float var = v / (float)cols;
+  const float inv = 1.0f / sqrtf(var + eps);
+  for (size_t c = 0; c < cols; ++c) row[c] = (row[c] - mean) * inv * gamma[c] + beta[c];
+}
+
+/* src/scalar.rs:83-95 */
+void vko_layernorm(float* x, size_t rows, size_t cols, const float* gamma, const float* beta,
+                   float eps) {
+#pragma omp parallel for schedule(static)
+  for (size_t r = 0; r < rows; ++r) layernorm_row(x + r * cols, cols, gamma, beta, eps);
+}
+
+/* src/scalar.rs:124-134: Abramowitz-Stegun 7.1.26.  Rust's signum is +1 for
+ * +0.0 and -1 for -0.0. */
+float vko_erf(float x) {
+  const float s = signbit(x) ? -1.0f : 1.0f;
+  x = fabsf(x);
+  const float t = 1.0f / (1.0f + 0.3275911f * x);
+  const float poly =
+      ((((1.0614054f * t - 1.453152f) * t) + 1.4214137f) * t - 0.28449674f) * t + 0.2548296f;
+  const float y = 1.0f - poly * t * expf(-x * x);
+  return s * y;
+}
+
+/* src/scalar.rs:116-121 */
+void vko_gelu(float* x, size_t n) {
+  const float inv_sqrt2 = 0.70710678118654752440f; /* std::f32::consts::FRAC_1_SQRT_2 */
+  for (size_t i = 0; i < n; ++i) {
+    const float v = x[i];
+    x[i] = 0.5f * v * (1.0f + vko_erf(v * inv_sqrt2));
+  }
+}
+
+/* src/scalar.rs:139-155 */
+void vko_layerscale(float* x, size_t rows, size_t cols, const float* gamma) {
+  for (size_t r = 0; r < rows; ++r)
+    for (size_t c = 0; c < cols; ++c) x[r * cols + c] *= gamma[c];
+}
+
+/* src/scalar.rs:157-172 */
+void vko_softmax_rows(float* x, size_t rows, size_t cols) {
+  for (size_t r = 0; r < rows; ++r) {
+    float* row = x + r * cols;
+    float m = -INFINITY;
+    for (size_t c = 0; c < cols; ++c) m = rs_max(m, row[c]);
+    float sum = 0.0f;
+    for (size_t c = 0; c < cols; ++c) {
+      row[c] = expf(row[c] - m);
+      sum += row[c];
+    }
+    const float inv = 1.0f / sum;
+    for (size_t c = 0; c < cols; ++c) row[c] *= inv;
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* src/attention.rs                                                    */
+/* ------------------------------------------------------------------ */
+
+static inline float dot_seq(const float* a, const float* b, size_t n) {
+  float s = -0.0f;
+  for (size_t i = 0; i < n; ++i) s += a[i] * b[i];
+  return s;
+}
+
+/* src/attention.rs:10-59.  Rows are independent; each keeps the reference
+ * order (scores, max, exp and sum over all n keys, then weighted V sum). */
+void vko_attention_naive(const float* q, const float* k, const float* v, size_t heads, size_t n,
+                         size_t head_dim, float* out) {
+  const float scale = 1.0f / sqrtf((float)head_dim);
+#pragma omp parallel
+  {
+    float* scores = (float*)malloc(sizeof(float) * (n ? n : 1));
+#pragma omp for schedule(static)
+    for (size_t row = 0; row < heads * n; ++row) {
+      const size_t h = row / n, i = row % n;
+      const float* qh = q + h * n * head_dim;
+      const float* kh = k + h * n * head_dim;
+      const float* vh = v + h * n * head_dim;
+      const float* qi = qh + i * head_dim;
+      float max_score = -INFINITY;
+      for (size_t j = 0; j < n; ++j) {
+        const float s = dot_seq(qi, kh + j * head_dim, head_dim) * scale;
+        scores[j] = s;
+        if (s > max_score) max_score = s;
+      }
+      float sum = 0.0f;
+      for (size_t j = 0; j < n; ++j) {
+        scores[j] = expf(scores[j] - max_score);
+        sum += scores[j];
+      }
+      const float inv_sum = 1.0f / sum;
+      float* oi = out + row * head_dim;
+      for (size_t d = 0; d < head_dim; ++d) oi[d] = 0.0f;
+      for (size_t j = 0; j < n; ++j) {
+        const float w = scores[j] * inv_sum;
+        const float* vj = vh + j * head_dim;
+        for (size_t d = 0; d < head_dim; ++d) oi[d] += w * vj[d];
+      }
+    }
+    free(scores);
+  }
+}
+
+#define VKO_KV_TILE 64
+
+/* src/attention.rs:111-201 with use_avx512 == false. */
+static void attention_row(const float* qh, const float* kh, const float* vh, size_t i, size_t n,
+                          size_t head_dim, float scale, float* acc, float* oi) {
+  const float* qi = qh + i * head_dim;
+  float running_max = -INFINITY;
+  float running_sum = 0.0f;
+  for (size_t d = 0; d < head_dim; ++d) acc[d] = 0.0f;
+  size_t j0 = 0;
+  while (j0 < n) {
+    const size_t j1 = (j0 + VKO_KV_TILE < n) ? j0 + VKO_KV_TILE : n;
+    float local[VKO_KV_TILE];
+    float tile_max = -INFINITY;
+    for (size_t j = j0; j < j1; ++j) {
+      const float score = dot_seq(qi, kh + j * head_dim, head_dim) * scale;
+      local[j - j0] = score;
+      if (score > tile_max) tile_max = score;
+    }
+    const float new_max = rs_max(running_max, tile_max);
+    const float correction = isfinite(running_max) ? expf(running_max - new_max) : 0.0f;
+    running_sum *= correction;
+    for (size_t d = 0; d < head_dim; ++d) acc[d] *= correction;
+    for (size_t t = 0; t < j1 - j0; ++t) local[t] -= new_max;
+    for (size_t t = 0; t < j1 - j0; ++t) local[t] = expf(local[t]);
+    for (size_t j = j0; j < j1; ++j) {
+      const float p = local[j - j0];
+      running_sum += p;
+      const float* vj = vh + j * head_dim;
+      for (size_t d = 0; d < head_dim; ++d) acc[d] += p * vj[d];
+    }
+    running_max = new_max;
+    j0 = j1;
+  }
+  const float inv_sum = 1.0f / running_sum;
+  for (size_t d = 0; d < head_dim; ++d) oi[d] = acc[d] * inv_sum;
+}
+
+/* src/attention.rs:66-108 (the tiled online route). */
+void vko_attention(const float* q, const float* k, const float* v, size_t heads, size_t n,
+                   size_t head_dim, float* out) {
+  const float scale = 1.0f / sqrtf((float)head_dim);
+#pragma omp parallel
+  {
+    float* acc = (float*)malloc(sizeof(float) * (head_dim ? head_dim : 1));
+#pragma omp for schedule(static)
+    for (size_t row = 0; row < heads * n; ++row) {
+      const size_t h = row / n, i = row % n;
+      const size_t base = h * n * head_dim;
+      attention_row(q + base, k + base, v + base, i, n, head_dim, scale, acc,
+                    out + row * head_dim);
+    }
+    free(acc);
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* RoPE: src/rope.rs and src/specialized.rs                            */
+/* ------------------------------------------------------------------ */
+
+/* src/rope.rs:84-93 */
+static void rotate_half(float* slice, size_t quarter, const float* rot) {
+  for (size_t i = 0; i < quarter; ++i) {
+    const float s = rot[i * 2], c = rot[i * 2 + 1];
+    const float a = slice[i], b = slice[i + quarter];
+    slice[i] = a * c - b * s;
+    slice[i + quarter] = b * c + a * s;
+  }
+}
+
+/* src/rope.rs:30-81 */
+void vko_rope2d(float* x, size_t heads, size_t n, size_t head_dim, const int64_t* pos_yx,
+                float freq) {
+  const size_t half_dim = head_dim / 2, quarter = half_dim / 2;
+  float* inv_freq = (float*)malloc(sizeof(float) * (quarter ? quarter : 1));
+  for (size_t i = 0; i < quarter; ++i)
+    inv_freq[i] = powf(freq, -2.0f * (float)i / (float)half_dim);
+  float* rot = (float*)malloc(sizeof(float) * (quarter ? 4 * quarter : 1));
+  for (size_t p = 0; p < n; ++p) {
+    const float pos[2] = {(float)pos_yx[2 * p], (float)pos_yx[2 * p + 1]};
+    for (int axis = 0; axis < 2; ++axis)
+      for (size_t i = 0; i < quarter; ++i) {
+        const float ang = pos[axis] * inv_freq[i];
+        rot[(axis * quarter + i) * 2] = sinf(ang);
+        rot[(axis * quarter + i) * 2 + 1] = cosf(ang);
+      }
+    for (size_t h = 0; h < heads; ++h) {
+      float* base = x + (h * n + p) * head_dim;
+      rotate_half(base, quarter, rot);
+      rotate_half(base + half_dim, quarter, rot + quarter * 2);
+    }
+  }
+  free(rot);
+  free(inv_freq);
+}
+
+/* src/specialized.rs:389-410 (QUARTER = 16, HALF_DIM = 32). */
+void vko_rope_rotations(const int64_t* pos_yx, size_t tokens, float freq, float* rotations) {
+  float inv_freq[16];
+  for (int i = 0; i < 16; ++i) inv_freq[i] = powf(freq, -2.0f * (float)i / 32.0f);
+  for (size_t t = 0; t < tokens; ++t)
+    for (int axis = 0; axis < 2; ++axis) {
+      const float pos = (float)pos_yx[2 * t + axis];
+      for (int i = 0; i < 16; ++i) {
+        const float ang = pos * inv_freq[i];
+        const size_t off = (t * 32 + (size_t)axis * 16 + (size_t)i) * 2;
+        rotations[off] = sinf(ang);
+        rotations[off + 1] = cosf(ang);
+      }
+    }
+}
+
+/* src/specialized.rs:412-454 */
+static void normalize_and_rotate(float* values, size_t rows, size_t tokens, const float* gamma,
+                                 const float* beta, float eps, const float* rot) {
+#pragma omp parallel for schedule(static)
+  for (size_t row = 0; row < rows; ++row) {
+    float* data = values + row * 64;
+    layernorm_row(data, 64, gamma, beta, eps);
+    const size_t token = row % tokens;
+    for (int axis = 0; axis < 2; ++axis) {
+      const float* r = rot + (token * 32 + (size_t)axis * 16) * 2;
+      rotate_half(data + axis * 32, 16, r);
+    }
+  }
+}
+
+void vko_qk_norm_rope(float* q, float* k, size_t heads, size_t tokens, const float* q_gamma,
+                      const float* q_beta, const float* k_gamma, const float* k_beta,
+                      const int64_t* pos_yx, float freq, float eps) {
+  float* rot = (float*)malloc(sizeof(float) * tokens * 64);
+  vko_rope_rotations(pos_yx, tokens, freq, rot);
+  normalize_and_rotate(q, heads * tokens, tokens, q_gamma, q_beta, eps, rot);
+  normalize_and_rotate(k, heads * tokens, tokens, k_gamma, k_beta, eps, rot);
+  free(rot);
+}
+
+void vko_da3_positions(size_t grid_h, size_t grid_w, int64_t* pos_yx) {
+  pos_yx[0] = 0;
+  pos_yx[1] = 0;
+  for (size_t p = 0; p < grid_h * grid_w; ++p) {
+    pos_yx[2 * (p + 1)] = (int64_t)(p / grid_w + 1);
+    pos_yx[2 * (p + 1) + 1] = (int64_t)(p % grid_w + 1);
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* Specialised projections (src/specialized.rs)                        */
+/* ------------------------------------------------------------------ */
+
+/* The specialised AVX-512 projections accumulate with one FMA per k in
+ * ascending order (src/specialized.rs:1133-1148, :943-955), which fmaf
+ * restates exactly. */
+static void gemm_fma_rows(size_t m, size_t n, size_t k, const float* a, const float* b,
+                          float* c) {
+#pragma omp parallel for schedule(static)
+  for (size_t i = 0; i < m; ++i) {
+    float* ci = c + i * n;
+    for (size_t j = 0; j < n; ++j) ci[j] = 0.0f;
+    for (size_t p = 0; p < k; ++p) {
+      const float aip = a[i * k + p];
+      const float* bp = b + p * n;
+      for (size_t j = 0; j < n; ++j) ci[j] = fmaf(aip, bp[j], ci[j]);
+    }
+  }
+}
+
+/* src/specialized.rs:1101-1167: acc + bias, stored head-major. */
+void vko_qkv(size_t tokens, size_t heads, const float* x, const float* w, const float* bias,
+             float* q, float* k, float* v) {
+  const size_t e = heads * 64, n3 = 3 * e;
+  float* tmp = (float*)malloc(sizeof(float) * tokens * n3);
+  gemm_fma_rows(tokens, n3, e, x, w, tmp);
+  for (size_t t = 0; t < tokens; ++t)
+    for (size_t col = 0; col < n3; ++col) {
+      const size_t g = col / e, h = (col % e) / 64, d = col % 64;
+      float* dst = g == 0 ? q : (g == 1 ? k : v);
+      dst[(h * tokens + t) * 64 + d] = tmp[t * n3 + col] + bias[col];
+    }
+  free(tmp);
+}
+
+/* src/specialized.rs:880-991: (acc + bias) * scale. */
+void vko_linear_bias_scale(size_t m, size_t n, size_t k, const float* a, const float* b,
+                           const float* bias, const float* scale, float* c) {
+  gemm_fma_rows(m, n, k, a, b, c);
+  for (size_t i = 0; i < m; ++i)
+    for (size_t j = 0; j < n; ++j) c[i * n + j] = (c[i * n + j] + bias[j]) * scale[j];
+}
+
+/* ------------------------------------------------------------------ */
+/* Engine-side block composition                                       */
+/* ------------------------------------------------------------------ */
+
+static void round_bf16_buf(float* x, size_t n) {
+  for (size_t i = 0; i < n; ++i) x[i] = vko_round_bf16(x[i]);
+}
+
+static float* copy_maybe_bf16(const float* src, size_t n, int bf16) {
+  float* d = (float*)malloc(sizeof(float) * n);
+  memcpy(d, src, sizeof(float) * n);
+  if (bf16) round_bf16_buf(d, n);
+  return d;
+}
+
+/* pre-LN -> QKV (+bias) -> 2D RoPE on Q,K (cls at (0,0), so unrotated) ->
+ * attention -> out-proj (+bias) * LS1 + residual -> LN -> fc1 (+bias) -> GELU
+ * -> fc2 (+bias) * LS2 + residual. */
+void vko_encoder_layer(float* x, size_t tokens, size_t grid_h, size_t grid_w, size_t embed,
+                       size_t heads, size_t ffn, const vko_layer* w, float eps, float rope_freq,
+                       int bf16_points) {
+  const size_t T = tokens, E = embed, F = ffn;
+  float* h = (float*)malloc(sizeof(float) * T * E);
+  float* q = (float*)malloc(sizeof(float) * T * E);
+  float* k = (float*)malloc(sizeof(float) * T * E);
+  float* v = (float*)malloc(sizeof(float) * T * E);
+  float* att = (float*)malloc(sizeof(float) * T * E);
+  float* tok = (float*)malloc(sizeof(float) * T * E);
+  float* o = (float*)malloc(sizeof(float) * T * E);
+  float* f = (float*)malloc(sizeof(float) * T * F);
+  int64_t* pos = (int64_t*)malloc(sizeof(int64_t) * 2 * T);
+  vko_da3_positions(grid_h, grid_w, pos);
+
+  float* wqkv = copy_maybe_bf16(w->qkv_w, E * 3 * E, bf16_points);
+  float* wo = copy_maybe_bf16(w->proj_w, E * E, bf16_points);
+  float* w1 = copy_maybe_bf16(w->fc1_w, E * F, bf16_points);
+  float* w2 = copy_maybe_bf16(w->fc2_w, F * E, bf16_points);
+
+  memcpy(h, x, sizeof(float) * T * E);
+  vko_layernorm(h, T, E, w->ln1_g, w->ln1_b, eps);
+  if (bf16_points) round_bf16_buf(h, T * E);
+  vko_qkv(T, heads, h, wqkv, w->qkv_b, q, k, v);
+  vko_rope2d(q, heads, T, 64, pos, rope_freq);
+  vko_rope2d(k, heads, T, 64, pos, rope_freq);
+  if (bf16_points) {
+    round_bf16_buf(q, T * E);
+    round_bf16_buf(k, T * E);
+    round_bf16_buf(v, T * E);
+  }
+  vko_attention_naive(q, k, v, heads, T, 64, att);
+  for (size_t hh = 0; hh < heads; ++hh)
+    for (size_t t = 0; t < T; ++t)
+      for (size_t d = 0; d < 64; ++d) tok[t * E + hh * 64 + d] = att[(hh * T + t) * 64 + d];
+  if (bf16_points) round_bf16_buf(tok, T * E);
+  vko_linear_bias_scale(T, E, E, tok, wo, w->proj_b, w->ls1, o);
+  vko_add(x, o, T * E);
+
+  memcpy(h, x, sizeof(float) * T * E);
+  vko_layernorm(h, T, E, w->ln2_g, w->ln2_b, eps);
+  if (bf16_points) round_bf16_buf(h, T * E);
+  gemm_fma_rows(T, F, E, h, w1, f);
+  vko_add_bias_rows(f, T, F, w->fc1_b);
+  vko_gelu(f, T * F);
+  if (bf16_points) round_bf16_buf(f, T * F);
+  vko_linear_bias_scale(T, E, F, f, w2, w->fc2_b, w->ls2, o);
+  vko_add(x, o, T * E);
+
+  free(wqkv); free(wo); free(w1); free(w2);
+  free(h); free(q); free(k); free(v); free(att); free(tok); free(o); free(f); free(pos);
+}

@@ -1,0 +1,124 @@
+/*
+ * vk_oracle.h -- CPU restatement of the vestra-kernels reference arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the parity checker for the
+ * B200 kernels: only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline / --impl reference legs may load it.  The product path
+ * (vestra-kernels_b200/) never links or calls it.
+ *
+ * Every function restates one reference function; the citation beside each
+ * declaration is the reference file:line it follows (paths are relative to
+ * the vestra-kernels crate root).  Evaluation order, rounding points and
+ * constants follow the reference so that outputs are bit-identical to the
+ * reference's scalar path on the same inputs (the reference crate cannot be
+ * built here: no Rust toolchain, and its registry dependencies are not
+ * vendored; see the "parity pin" notes in the test files).
+ */
+#ifndef VK_ORACLE_H
+#define VK_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VKO_QK8_0 32
+
+/* BlockQ8_0 {d: f16, qs: [i8;32]}, #[repr(C)], 34 bytes (src/lib.rs:33-38). */
+typedef struct __attribute__((packed)) {
+  uint16_t d;
+  int8_t qs[VKO_QK8_0];
+} vko_block_q8_0;
+
+/* IEEE binary16 round-to-nearest-even, as half::f16::from_f32 (half 2.7.1). */
+uint16_t vko_f16_from_f32(float x);
+float vko_f16_to_f32(uint16_t h);
+/* bfloat16 round-to-nearest-even (the rounding the B200 kernels apply). */
+float vko_round_bf16(float x);
+
+/* src/scalar.rs:3-18 */
+void vko_gemm_f32(size_t m, size_t n, size_t k, const float* a, const float* b, float* c);
+/* src/scalar.rs:25-56 */
+void vko_gemm_q8_0(size_t m, size_t n, size_t k, const vko_block_q8_0* a_q,
+                   const vko_block_q8_0* b_q, float* c);
+/* The int32 block dot of src/scalar.rs:47-50, exposed so the int32 sums can
+ * be checked bit for bit: out[(i*n+j)*nb + b] = sum_l qa*qb. */
+void vko_q8_0_block_dots(size_t m, size_t n, size_t k, const vko_block_q8_0* a_q,
+                         const vko_block_q8_0* b_q, int32_t* out);
+/* src/lib.rs:42-50 */
+void vko_dequantize_q8_0(const vko_block_q8_0* blocks, size_t nblocks, float* out);
+/* src/q8_0_dot.rs:27-46 */
+void vko_quantize_row_q8_0(const float* x, size_t nblocks, vko_block_q8_0* out);
+
+/* src/scalar.rs:58-63 */
+void vko_add(float* dst, const float* src, size_t n);
+/* src/scalar.rs:65-81 */
+void vko_add_bias_rows(float* x, size_t rows, size_t cols, const float* bias);
+/* src/scalar.rs:83-114 */
+void vko_layernorm(float* x, size_t rows, size_t cols, const float* gamma, const float* beta,
+                   float eps);
+/* src/scalar.rs:116-134 */
+void vko_gelu(float* x, size_t n);
+float vko_erf(float x);
+/* src/scalar.rs:139-155 */
+void vko_layerscale(float* x, size_t rows, size_t cols, const float* gamma);
+/* src/scalar.rs:157-172 */
+void vko_softmax_rows(float* x, size_t rows, size_t cols);
+
+/* src/attention.rs:10-59 */
+void vko_attention_naive(const float* q, const float* k, const float* v, size_t heads, size_t n,
+                         size_t head_dim, float* out);
+/* src/attention.rs:66-201, scalar route (use_avx512 == false, as attention_serial) */
+void vko_attention(const float* q, const float* k, const float* v, size_t heads, size_t n,
+                   size_t head_dim, float* out);
+
+/* src/rope.rs:30-93 */
+void vko_rope2d(float* x, size_t heads, size_t n, size_t head_dim, const int64_t* pos_yx,
+                float freq);
+/* src/specialized.rs:389-410: rotations[(t*2*16 + axis*16 + i)*2 + {0:sin,1:cos}] */
+void vko_rope_rotations(const int64_t* pos_yx, size_t tokens, float freq, float* rotations);
+/* src/specialized.rs:278-318, 412-454 (generalised over token count) */
+void vko_qk_norm_rope(float* q, float* k, size_t heads, size_t tokens, const float* q_gamma,
+                      const float* q_beta, const float* k_gamma, const float* k_beta,
+                      const int64_t* pos_yx, float freq, float eps);
+/* DA3 position layout, src/specialized.rs:359-366 generalised to a grid of
+ * width grid_w: cls token (0,0), patch p -> (p / grid_w + 1, p % grid_w + 1). */
+void vko_da3_positions(size_t grid_h, size_t grid_w, int64_t* pos_yx);
+
+/* src/specialized.rs:996-1167: q/k/v[h,t,:] = x[t,:] . W[:, g*768 + h*64 ..] + b,
+ * generalised to `tokens` rows and `heads` x 64 columns per group. */
+void vko_qkv(size_t tokens, size_t heads, const float* x, const float* w, const float* bias,
+             float* q, float* k, float* v);
+/* src/specialized.rs:811-991: c = (a.b + bias) * scale */
+void vko_linear_bias_scale(size_t m, size_t n, size_t k, const float* a, const float* b,
+                           const float* bias, const float* scale, float* c);
+
+/* One DA3-BASE ViT block composed from the restated operators (the engine's
+ * composition, which is not in the reference crate).  When bf16_points is
+ * non-zero the inputs of every matrix product and the tensors the B200
+ * kernels store in bf16 are rounded to bf16 at the same points. */
+typedef struct {
+  const float *ln1_g, *ln1_b;
+  const float *qkv_w, *qkv_b;   /* [E, 3E], [3E] */
+  const float *proj_w, *proj_b; /* [E, E], [E] */
+  const float* ls1;             /* [E] */
+  const float *ln2_g, *ln2_b;
+  const float *fc1_w, *fc1_b;   /* [E, F], [F] */
+  const float *fc2_w, *fc2_b;   /* [F, E], [E] */
+  const float* ls2;             /* [E] */
+} vko_layer;
+
+void vko_encoder_layer(float* x, size_t tokens, size_t grid_h, size_t grid_w, size_t embed,
+                       size_t heads, size_t ffn, const vko_layer* w, float eps, float rope_freq,
+                       int bf16_points);
+
+/* Threads used by the parallel loops (rows are independent and each keeps
+ * the scalar reduction order, so results do not depend on this). */
+void vko_set_threads(int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
