@@ -1,0 +1,195 @@
+/*
+ * vestra_b200.h -- C ABI of the B200 (sm_100a) DA3-BASE encoder hot path.
+ *
+ * Drop-in for the primitive-buffer API of the vestra-kernels crate
+ * (API.md:1-16, src/lib.rs:1-132).  Conventions:
+ *  - every entry point returns an int status; VK_UNSUPPORTED_SHAPE plays the
+ *    role of the reference's `false` ("shape unsupported, use your
+ *    fallback") and leaves outputs untouched; vk_last_error() describes the
+ *    last failure of the calling thread;
+ *  - buffers are caller-owned plain pointers with explicit dimensions;
+ *    "dev" pointers are device memory of the context's GPU, "host" pointers
+ *    host memory (pageable or pinned);
+ *  - operations are enqueued on the context's stream (vk_stream_set) and
+ *    are asynchronous; vk_synchronize() waits and reports device-side
+ *    timeouts (VK_ERR_TIMEOUT);
+ *  - one context per GPU; a context is not shared between threads without
+ *    external synchronisation;
+ *  - weights use the reference layout: [K, N] row-major, input-major
+ *    (src/specialized.rs:1058, b[kk * n + col]).
+ * Nothing in this header uses C++ or CUDA types.
+ */
+#ifndef VESTRA_B200_H
+#define VESTRA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VK_OK 0
+#define VK_UNSUPPORTED_SHAPE 1
+#define VK_ERR_INVALID_ARGUMENT 2
+#define VK_ERR_CUDA 3
+#define VK_ERR_TIMEOUT 4
+#define VK_ERR_NO_DEVICE 5
+#define VK_ERR_OUT_OF_MEMORY 6
+
+/* Arithmetic of the f32-interface operators and of an encoder. */
+#define VK_MATH_F32 0  /* f32 in, f32 arithmetic (CUDA cores), f32 out      */
+#define VK_MATH_BF16 1 /* bf16 tensor-core products, f32 accumulation        */
+#define VK_MATH_Q8_0 2 /* Q8_0 weights and activations, int8 tensor cores   */
+
+typedef struct vk_ctx vk_ctx;
+typedef struct vk_linear vk_linear;
+typedef struct vk_encoder vk_encoder;
+
+/* 34-byte Q8_0 record, identical to BlockQ8_0 {d: f16, qs: [i8; 32]}
+ * (#[repr(C)], src/lib.rs:33-38). */
+#define VK_QK8_0 32
+typedef struct {
+  uint16_t d;
+  int8_t qs[VK_QK8_0];
+} vk_block_q8_0;
+
+/* ---------------------------------------------------------------- lifecycle */
+/* Context on CUDA device `device` (one per GPU).  Replaces CudaRuntime::new
+ * (src/cuda.rs:383-443). */
+int vk_init(int device, vk_ctx** out);
+int vk_destroy(vk_ctx* ctx);
+/* Use this cudaStream_t (NULL = legacy default stream) for later calls. */
+int vk_stream_set(vk_ctx* ctx, void* stream);
+/* Arithmetic of the f32-interface operators below (default VK_MATH_F32). */
+int vk_set_math(vk_ctx* ctx, int math);
+/* Waits for the context's stream; VK_ERR_TIMEOUT if a kernel gave up a wait. */
+int vk_synchronize(vk_ctx* ctx);
+const char* vk_last_error(void);
+const char* vk_version(void);
+
+/* ------------------------------------------- DA3-BASE specialised operators
+ * Device pointers.  These replace the five `*_da3_base` functions of
+ * src/lib.rs.  The reference gates them to 865 tokens; here any token count
+ * >= 1 is accepted (the 3457-token configuration included). */
+
+/* src/lib.rs:52 qkv_f32_da3_base: input [tokens, 768], weight [768, 2304],
+ * bias [2304] -> q, k, v [12, tokens, 64] head-major (bias added, no RoPE). */
+int vk_qkv_f32_da3_base(vk_ctx* ctx, size_t tokens, const float* input, const float* weight,
+                        const float* bias, float* q, float* k, float* v);
+
+/* src/lib.rs:67 linear_f32_da3_base: output[m, n] = input[m, k] . weight[k, n].
+ * (k, n) must be a DA3-BASE projection: (768, 2304), (768, 768), (768, 3072)
+ * or (3072, 768). */
+int vk_linear_f32_da3_base(vk_ctx* ctx, size_t m, size_t n, size_t k, const float* input,
+                           const float* weight, float* output);
+
+/* src/lib.rs:94 linear_bias_scale_f32_da3_base: c = (a . b + bias) * scale,
+ * (k, n) in {(768, 768), (3072, 768)}. */
+int vk_linear_bias_scale_f32_da3_base(vk_ctx* ctx, size_t m, size_t n, size_t k, const float* a,
+                                      const float* b, const float* bias, const float* scale,
+                                      float* c);
+
+/* src/lib.rs:82 flash_attention_f32_da3_base: q, k, v, out [heads, tokens, 64]. */
+int vk_flash_attention_f32_da3_base(vk_ctx* ctx, const float* query, const float* key,
+                                    const float* value, size_t heads, size_t tokens,
+                                    float* output);
+
+/* src/lib.rs:108 qk_norm_rope_f32_da3_base: in place on q, k [heads, tokens, 64];
+ * gamma/beta [64]; positions_yx int64 [tokens, 2] (device). */
+int vk_qk_norm_rope_f32_da3_base(vk_ctx* ctx, float* q, float* k, size_t heads, size_t tokens,
+                                 const float* q_gamma, const float* q_beta, const float* k_gamma,
+                                 const float* k_beta, const int64_t* positions_yx,
+                                 float frequency, float epsilon);
+
+/* ------------------------------------------------------ generic operators */
+/* src/attention.rs:66 attention: q, k, v, out [heads, n, head_dim]; head_dim
+ * in {8, 16, 32, 64} (64 follows vk_set_math, others are f32). */
+int vk_attention(vk_ctx* ctx, const float* q, const float* k, const float* v, size_t heads,
+                 size_t n, size_t head_dim, float* out);
+/* src/rope.rs:30 rope2d, in place on x [heads, n, head_dim], head_dim % 4 == 0,
+ * pos_yx int64 [n, 2] (device). */
+int vk_rope2d(vk_ctx* ctx, float* x, size_t heads, size_t n, size_t head_dim,
+              const int64_t* pos_yx, float freq);
+/* src/scalar.rs:83 layernorm, in place on x [rows, cols]. */
+int vk_layernorm(vk_ctx* ctx, float* x, size_t rows, size_t cols, const float* gamma,
+                 const float* beta, float eps);
+/* src/dispatch.rs:56 Kernels::gelu (exact-erf GELU, A&S 7.1.26), in place. */
+int vk_gelu(vk_ctx* ctx, float* x, size_t n);
+/* src/dispatch.rs:77 Kernels::add: dst += src. */
+int vk_add(vk_ctx* ctx, float* dst, const float* src, size_t n);
+/* src/scalar.rs:65 add_bias_rows, src/scalar.rs:139 layerscale. */
+int vk_add_bias_rows(vk_ctx* ctx, float* x, size_t rows, size_t cols, const float* bias);
+int vk_layerscale(vk_ctx* ctx, float* x, size_t rows, size_t cols, const float* gamma);
+/* src/q8_0_dot.rs:27 quantize_row_q8_0: x [nblocks * 32] -> out [nblocks]. */
+int vk_quantize_row_q8_0(vk_ctx* ctx, const float* x, size_t nblocks, vk_block_q8_0* out);
+/* src/dispatch.rs:91 Kernels::gemm_q8_0: a_q [m, k/32], b_q [n, k/32]
+ * (B pre-transposed, as in the reference), c [m, n] f32.  k % 128 == 0,
+ * n % 128 == 0. */
+int vk_gemm_q8_0(vk_ctx* ctx, size_t m, size_t n, size_t k, const vk_block_q8_0* a_q,
+                 const vk_block_q8_0* b_q, float* c);
+/* The int32 block dot products of the same kernel, out [m, n, k/32]
+ * (src/scalar.rs:47-50), for bit-exact verification. */
+int vk_gemm_q8_0_block_dots(vk_ctx* ctx, size_t m, size_t n, size_t k,
+                            const vk_block_q8_0* a_q, const vk_block_q8_0* b_q, int32_t* dots);
+
+/* --------------------------------------------------------- prepared values
+ * Mirrors the prepared-value objects of the reference (CudaLinearF32,
+ * src/cuda.rs:1233-1334): weights are converted and laid out once. */
+/* weight_host [k, n] f32, bias_host / scale_host [n] or NULL; math selects
+ * the stored form (f32, bf16, or Q8_0 quantised per 32 along k). */
+int vk_prepare_linear(vk_ctx* ctx, size_t k, size_t n, const float* weight_host,
+                      const float* bias_host, const float* scale_host, int math,
+                      vk_linear** out);
+/* Q8_0 weights given as blocks [n, k/32] (host). */
+int vk_prepare_linear_q8_0(vk_ctx* ctx, size_t k, size_t n, const vk_block_q8_0* blocks_host,
+                           const float* bias_host, const float* scale_host, vk_linear** out);
+/* output[m, n] = (input[m, k] . W + bias) * scale, device pointers. */
+int vk_linear_run(vk_ctx* ctx, const vk_linear* lin, size_t m, const float* input, float* output);
+int vk_release_linear(vk_linear* lin);
+
+/* ------------------------------------------------------------- encoder
+ * DA3-BASE ViT encoder: pre-LN -> QKV -> 2D RoPE on Q, K (cls unrotated) ->
+ * attention -> out-proj + LayerScale + residual -> LN -> fc1 + GELU -> fc2 +
+ * LayerScale + residual, for `layers` blocks (the composition the engine
+ * performs with the operators above). */
+typedef struct {
+  const float *ln1_gamma, *ln1_beta;     /* [E]            */
+  const float *qkv_weight, *qkv_bias;    /* [E, 3E], [3E]  */
+  const float *proj_weight, *proj_bias;  /* [E, E], [E]    */
+  const float* ls1;                      /* [E]            */
+  const float *ln2_gamma, *ln2_beta;     /* [E]            */
+  const float *fc1_weight, *fc1_bias;    /* [E, F], [F]    */
+  const float *fc2_weight, *fc2_bias;    /* [F, E], [E]    */
+  const float* ls2;                      /* [E]            */
+} vk_layer_weights;
+
+typedef struct {
+  int layers;      /* 12 for DA3-BASE                */
+  int heads;       /* 12; embed = heads * 64         */
+  int ffn;         /* 3072                           */
+  float eps;       /* LayerNorm epsilon, 1e-6        */
+  float rope_freq; /* 100                            */
+  int math;        /* VK_MATH_BF16, VK_MATH_Q8_0 or VK_MATH_F32 */
+} vk_encoder_config;
+
+/* layers_host[cfg->layers], host f32 in the reference layout. */
+int vk_encoder_prepare(vk_ctx* ctx, const vk_encoder_config* cfg,
+                       const vk_layer_weights* layers_host, vk_encoder** out);
+/* tokens / out: [images, 1 + grid_h * grid_w, E] f32, device pointers (may
+ * alias).  Token 0 of each image is the cls token at RoPE position (0, 0);
+ * patch p sits at (p / grid_w + 1, p % grid_w + 1). */
+int vk_encoder_forward(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h, size_t grid_w,
+                       const float* tokens_dev, float* out_dev);
+/* Same with host buffers: the copies in and out are pipelined with the
+ * compute in image chunks (the end-to-end entry point). */
+int vk_encoder_forward_host(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h,
+                            size_t grid_w, const float* tokens_host, float* out_host);
+/* Kernels launched by the last vk_encoder_forward (for accounting). */
+int vk_encoder_last_launches(const vk_encoder* enc);
+int vk_encoder_release(vk_encoder* enc);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,411 @@
+// vk_elementwise.cu -- the HBM-bound kernels of the path: LayerNorm (with
+// bf16 / Q8_0 output fused), RoPE, Q/K-norm+RoPE, Q8_0 quantisation and the
+// stand-alone epilogue passes of the reference's f32 API.
+//
+// Reference functions restated (file:line in the vestra-kernels crate):
+//   layernorm            src/scalar.rs:83-114
+//   gelu / erf           src/scalar.rs:116-134, src/dispatch.rs:56-73
+//   add                  src/dispatch.rs:77, src/scalar.rs:58-63
+//   add_bias_rows        src/scalar.rs:65-81
+//   layerscale           src/scalar.rs:139-155
+//   rope2d               src/rope.rs:30-93
+//   qk_norm_rope         src/specialized.rs:278-454
+//   quantize_row_q8_0    src/q8_0_dot.rs:27-46
+#include "vk_common.cuh"
+#include "vk_internal.h"
+
+namespace vk {
+
+namespace {
+constexpr int EW_THREADS = 256;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+inline int ew_grid(size_t n) {
+  size_t g = (n + EW_THREADS - 1) / EW_THREADS;
+  const size_t cap = static_cast<size_t>(num_sms()) * 16;
+  return static_cast<int>(g < cap ? (g ? g : 1) : cap);
+}
+}  // namespace
+
+// ---------------------------------------------------------------- LayerNorm
+// One warp per row; the row stays in registers between the two passes (mean,
+// then mean of squared deviations, as src/scalar.rs:99-110).  Output f32, bf16
+// or Q8_0 blocks (amax over the 8 lanes that hold one 32-block).
+template <int VPL>  // float4 vectors per lane; cols == VPL * 128
+__global__ void __launch_bounds__(EW_THREADS)
+    k_layernorm_vec(const float* __restrict__ x, float* y, __nv_bfloat16* yb, int8_t* yq, __half* yd,
+                    int rows, int cols, const float* __restrict__ g, const float* __restrict__ b, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(warp) * cols);
+  float4 v[VPL];
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    v[j] = __ldg(xr + j * 32 + lane);
+    s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+  }
+  const float mean = warp_sum(s) / static_cast<float>(cols);
+  float q = 0.0f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const float a = v[j].x - mean, bb = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
+    q += (a * a + bb * bb) + (c * c + d * d);
+  }
+  const float var = warp_sum(q) / static_cast<float>(cols);
+  const float inv = 1.0f / sqrtf(var + eps);
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int c0 = (j * 32 + lane) * 4;
+    const float4 gg = __ldg(reinterpret_cast<const float4*>(g + c0));
+    const float4 bt = __ldg(reinterpret_cast<const float4*>(b + c0));
+    float4 o;
+    o.x = (v[j].x - mean) * inv * gg.x + bt.x;
+    o.y = (v[j].y - mean) * inv * gg.y + bt.y;
+    o.z = (v[j].z - mean) * inv * gg.z + bt.z;
+    o.w = (v[j].w - mean) * inv * gg.w + bt.w;
+    const size_t off = static_cast<size_t>(warp) * cols + c0;
+    if (y != nullptr) *reinterpret_cast<float4*>(y + off) = o;
+    if (yb != nullptr) *reinterpret_cast<uint2*>(yb + off) = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
+    if (yq != nullptr) {
+      // 8 consecutive lanes hold one 32-wide Q8_0 block.
+      float amax = fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w)));
+#pragma unroll
+      for (int m = 1; m < 8; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+      const float dd = amax / 127.0f;
+      const float id = dd != 0.0f ? 1.0f / dd : 0.0f;
+      char4 qq;
+      qq.x = static_cast<signed char>(fminf(fmaxf(roundf(o.x * id), -127.0f), 127.0f));
+      qq.y = static_cast<signed char>(fminf(fmaxf(roundf(o.y * id), -127.0f), 127.0f));
+      qq.z = static_cast<signed char>(fminf(fmaxf(roundf(o.z * id), -127.0f), 127.0f));
+      qq.w = static_cast<signed char>(fminf(fmaxf(roundf(o.w * id), -127.0f), 127.0f));
+      *reinterpret_cast<char4*>(yq + off) = qq;
+      if ((lane & 7) == 0) yd[off / 32] = __float2half_rn(dd);
+    }
+  }
+}
+
+// Generic row length: one warp per row, three passes over global memory.
+__global__ void k_layernorm_generic(const float* __restrict__ x, float* y, int rows, int cols,
+                                    const float* __restrict__ g, const float* __restrict__ b, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float* xr = x + static_cast<size_t>(warp) * cols;
+  float s = 0.0f;
+  for (int c = lane; c < cols; c += 32) s += xr[c];
+  const float mean = warp_sum(s) / static_cast<float>(cols);
+  float q = 0.0f;
+  for (int c = lane; c < cols; c += 32) {
+    const float d = xr[c] - mean;
+    q += d * d;
+  }
+  const float var = warp_sum(q) / static_cast<float>(cols);
+  const float inv = 1.0f / sqrtf(var + eps);
+  float* yr = y + static_cast<size_t>(warp) * cols;
+  for (int c = lane; c < cols; c += 32) yr[c] = (xr[c] - mean) * inv * g[c] + b[c];
+}
+
+cudaError_t layernorm_f32(const float* x, float* y, __nv_bfloat16* yb, int8_t* yq, __half* yd, int rows, int cols,
+                          const float* g, const float* b, float eps, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  const int grid = (rows * 32 + EW_THREADS - 1) / EW_THREADS;
+  const bool vec_ok = (cols % 128 == 0) && cols <= 1024 &&
+                      (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(g) % 16 == 0) &&
+                      (reinterpret_cast<uintptr_t>(b) % 16 == 0);
+  if (!vec_ok) {
+    if (yb != nullptr || yq != nullptr || y == nullptr) return cudaErrorInvalidValue;
+    k_layernorm_generic<<<grid, EW_THREADS, 0, s>>>(x, y, rows, cols, g, b, eps);
+    return cudaGetLastError();
+  }
+  switch (cols / 128) {
+#define VK_LN_CASE(n) \
+  case n: k_layernorm_vec<n><<<grid, EW_THREADS, 0, s>>>(x, y, yb, yq, yd, rows, cols, g, b, eps); break;
+    VK_LN_CASE(1) VK_LN_CASE(2) VK_LN_CASE(3) VK_LN_CASE(4) VK_LN_CASE(5) VK_LN_CASE(6) VK_LN_CASE(7)
+    VK_LN_CASE(8)
+#undef VK_LN_CASE
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- pointwise
+__global__ void k_gelu(float* x, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    x[i] = gelu_erf(x[i]);
+}
+cudaError_t gelu_f32(float* x, size_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  k_gelu<<<ew_grid(n), EW_THREADS, 0, s>>>(x, n);
+  return cudaGetLastError();
+}
+
+__global__ void k_add(float* dst, const float* src, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = dst[i] + src[i];
+}
+cudaError_t add_f32(float* dst, const float* src, size_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  k_add<<<ew_grid(n), EW_THREADS, 0, s>>>(dst, src, n);
+  return cudaGetLastError();
+}
+
+__global__ void k_bias_rows(float* x, size_t rows, size_t cols, const float* bias) {
+  const size_t n = rows * cols;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    x[i] = x[i] + bias[i % cols];
+}
+cudaError_t add_bias_rows_f32(float* x, size_t rows, size_t cols, const float* bias, cudaStream_t s) {
+  if (rows * cols == 0) return cudaSuccess;
+  k_bias_rows<<<ew_grid(rows * cols), EW_THREADS, 0, s>>>(x, rows, cols, bias);
+  return cudaGetLastError();
+}
+
+__global__ void k_layerscale(float* x, size_t rows, size_t cols, const float* g) {
+  const size_t n = rows * cols;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    x[i] = x[i] * g[i % cols];
+}
+cudaError_t layerscale_f32(float* x, size_t rows, size_t cols, const float* g, cudaStream_t s) {
+  if (rows * cols == 0) return cudaSuccess;
+  k_layerscale<<<ew_grid(rows * cols), EW_THREADS, 0, s>>>(x, rows, cols, g);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- RoPE
+// One thread per rotation pair.  rot[(t * 2 * quarter + axis * quarter + i) * 2 + {0: sin, 1: cos}]
+// as in src/rope.rs:49-60.  Products and sums are separately rounded (no FMA
+// contraction), so the result is bit-identical to the reference's rotate_half.
+__global__ void k_rope2d(float* x, int heads, int n, int head_dim, const float* __restrict__ rot) {
+  const int quarter = head_dim / 4, half = head_dim / 2;
+  const size_t total = static_cast<size_t>(heads) * n * 2 * quarter;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(idx % quarter);
+    const int axis = static_cast<int>((idx / quarter) % 2);
+    const size_t ht = idx / (2 * quarter);  // h * n + p
+    const int p = static_cast<int>(ht % n);
+    float* base = x + ht * head_dim + axis * half;
+    const float sn = rot[(static_cast<size_t>(p) * 2 * quarter + axis * quarter + i) * 2];
+    const float cs = rot[(static_cast<size_t>(p) * 2 * quarter + axis * quarter + i) * 2 + 1];
+    const float a = base[i], b = base[i + quarter];
+    base[i] = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+    base[i + quarter] = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+  }
+}
+cudaError_t rope2d_f32(float* x, int heads, int n, int head_dim, const float* rot, cudaStream_t s) {
+  const size_t total = static_cast<size_t>(heads) * n * (head_dim / 2);
+  if (total == 0) return cudaSuccess;
+  k_rope2d<<<ew_grid(total), EW_THREADS, 0, s>>>(x, heads, n, head_dim, rot);
+  return cudaGetLastError();
+}
+
+// Fused Q/K LayerNorm (64-wide rows) + axial RoPE: one warp per row, lane l
+// holds dims l and l + 32; the rotation partner of dim d is d ^ 16.
+__global__ void k_qk_norm_rope(float* q, float* k, int rows, int tokens, const float* __restrict__ qg,
+                               const float* __restrict__ qb, const float* __restrict__ kg,
+                               const float* __restrict__ kb, const float* __restrict__ rot, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= 2 * rows) return;
+  const bool is_k = warp >= rows;
+  const int row = is_k ? warp - rows : warp;
+  float* data = (is_k ? k : q) + static_cast<size_t>(row) * 64;
+  const float* g = is_k ? kg : qg;
+  const float* bt = is_k ? kb : qb;
+  float x0 = data[lane], x1 = data[lane + 32];
+  const float mean = warp_sum(x0 + x1) / 64.0f;
+  const float d0 = x0 - mean, d1 = x1 - mean;
+  const float var = warp_sum(d0 * d0 + d1 * d1) / 64.0f;
+  const float inv = 1.0f / sqrtf(var + eps);
+  x0 = __fadd_rn(__fmul_rn(__fmul_rn(d0, inv), g[lane]), bt[lane]);
+  x1 = __fadd_rn(__fmul_rn(__fmul_rn(d1, inv), g[lane + 32]), bt[lane + 32]);
+  const float p0 = __shfl_xor_sync(0xffffffffu, x0, 16);
+  const float p1 = __shfl_xor_sync(0xffffffffu, x1, 16);
+  const int token = row % tokens;
+  const int i = lane & 15;
+  const bool first = lane < 16;
+  // axis 0 for dims 0..31 (x0), axis 1 for dims 32..63 (x1)
+  const float* r0 = rot + (static_cast<size_t>(token) * 32 + i) * 2;
+  const float* r1 = rot + (static_cast<size_t>(token) * 32 + 16 + i) * 2;
+  const float s0 = r0[0], c0 = r0[1], s1 = r1[0], c1 = r1[1];
+  float y0, y1;
+  if (first) {
+    y0 = __fsub_rn(__fmul_rn(x0, c0), __fmul_rn(p0, s0));
+    y1 = __fsub_rn(__fmul_rn(x1, c1), __fmul_rn(p1, s1));
+  } else {
+    y0 = __fadd_rn(__fmul_rn(x0, c0), __fmul_rn(p0, s0));
+    y1 = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(p1, s1));
+  }
+  data[lane] = y0;
+  data[lane + 32] = y1;
+}
+cudaError_t qk_norm_rope_f32(float* q, float* k, int heads, int tokens, const float* qg, const float* qb,
+                             const float* kg, const float* kb, const float* rot, float eps, cudaStream_t s) {
+  const int rows = heads * tokens;
+  if (rows == 0) return cudaSuccess;
+  const int grid = (2 * rows * 32 + EW_THREADS - 1) / EW_THREADS;
+  k_qk_norm_rope<<<grid, EW_THREADS, 0, s>>>(q, k, rows, tokens, qg, qb, kg, kb, rot, eps);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- Q8_0
+// One thread per 32-block; d = amax / 127 (f32), inv from the f32 d, round
+// half away from zero, clamp to +-127 (src/q8_0_dot.rs:34-45).
+__global__ void k_quantize_q8_0(const float* __restrict__ x, size_t nblocks, int8_t* qs, __half* d) {
+  for (size_t bi = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; bi < nblocks;
+       bi += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float4* src = reinterpret_cast<const float4*>(x + bi * 32);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 f = __ldg(src + j);
+      v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    const float dd = amax / 127.0f;
+    const float id = dd != 0.0f ? 1.0f / dd : 0.0f;
+    d[bi] = __float2half_rn(dd);
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t packed = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float qf = fminf(fmaxf(roundf(v[4 * j + t] * id), -127.0f), 127.0f);
+        packed |= (static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xffu) << (8 * t);
+      }
+      w[j] = packed;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(qs + bi * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+cudaError_t quantize_q8_0(const float* x, size_t nblocks, int8_t* qs, __half* d, cudaStream_t s) {
+  if (nblocks == 0) return cudaSuccess;
+  k_quantize_q8_0<<<ew_grid(nblocks), EW_THREADS, 0, s>>>(x, nblocks, qs, d);
+  return cudaGetLastError();
+}
+
+// BlockQ8_0 records (34 bytes: f16 d, then 32 int8) <-> split arrays.
+__global__ void k_pack_q8(const int8_t* qs, const __half* d, size_t nblocks, uint8_t* blocks) {
+  const size_t total = nblocks * 34;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t b = i / 34, o = i % 34;
+    uint8_t val;
+    if (o < 2) {
+      const uint16_t h = __half_as_ushort(d[b]);
+      val = static_cast<uint8_t>(o == 0 ? (h & 0xff) : (h >> 8));
+    } else {
+      val = static_cast<uint8_t>(qs[b * 32 + (o - 2)]);
+    }
+    blocks[i] = val;
+  }
+}
+__global__ void k_unpack_q8(const uint8_t* blocks, size_t nblocks, int8_t* qs, __half* d) {
+  const size_t total = nblocks * 34;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t b = i / 34, o = i % 34;
+    if (o == 0) {
+      const uint16_t h = static_cast<uint16_t>(blocks[i]) | (static_cast<uint16_t>(blocks[i + 1]) << 8);
+      d[b] = __ushort_as_half(h);
+    } else if (o >= 2) {
+      qs[b * 32 + (o - 2)] = static_cast<int8_t>(blocks[i]);
+    }
+  }
+}
+cudaError_t pack_blocks_q8_0(const int8_t* qs, const __half* d, size_t nblocks, void* blocks, cudaStream_t s) {
+  if (nblocks == 0) return cudaSuccess;
+  k_pack_q8<<<ew_grid(nblocks * 34), EW_THREADS, 0, s>>>(qs, d, nblocks, static_cast<uint8_t*>(blocks));
+  return cudaGetLastError();
+}
+cudaError_t unpack_blocks_q8_0(const void* blocks, size_t nblocks, int8_t* qs, __half* d, cudaStream_t s) {
+  if (nblocks == 0) return cudaSuccess;
+  k_unpack_q8<<<ew_grid(nblocks * 34), EW_THREADS, 0, s>>>(static_cast<const uint8_t*>(blocks), nblocks, qs, d);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- layouts
+__global__ void k_cast_bf16(const float* x, __nv_bfloat16* y, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    y[i] = __float2bfloat16_rn(x[i]);
+}
+cudaError_t cast_f32_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  k_cast_bf16<<<ew_grid(n), EW_THREADS, 0, s>>>(x, y, n);
+  return cudaGetLastError();
+}
+
+// w [K, N] f32 -> wt [N, K] bf16 through a 32 x 33 shared tile.
+__global__ void k_transpose_cast(const float* __restrict__ w, __nv_bfloat16* wt, int K, int N) {
+  __shared__ float tile[32][33];
+  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int kk = k0 + r, nn = n0 + threadIdx.x;
+    tile[r][threadIdx.x] = (kk < K && nn < N) ? w[static_cast<size_t>(kk) * N + nn] : 0.0f;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int nn = n0 + r, kk = k0 + threadIdx.x;
+    if (nn < N && kk < K) wt[static_cast<size_t>(nn) * K + kk] = __float2bfloat16_rn(tile[threadIdx.x][r]);
+  }
+}
+cudaError_t transpose_cast_bf16(const float* w, __nv_bfloat16* wt, int K, int N, cudaStream_t s) {
+  dim3 grid((N + 31) / 32, (K + 31) / 32), block(32, 8);
+  k_transpose_cast<<<grid, block, 0, s>>>(w, wt, K, N);
+  return cudaGetLastError();
+}
+
+// w [K, N] f32 -> wt [N, K] f32.
+__global__ void k_transpose_f32(const float* __restrict__ w, float* wt, int K, int N) {
+  __shared__ float tile[32][33];
+  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int kk = k0 + r, nn = n0 + threadIdx.x;
+    tile[r][threadIdx.x] = (kk < K && nn < N) ? w[static_cast<size_t>(kk) * N + nn] : 0.0f;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int nn = n0 + r, kk = k0 + threadIdx.x;
+    if (nn < N && kk < K) wt[static_cast<size_t>(nn) * K + kk] = tile[threadIdx.x][r];
+  }
+}
+cudaError_t transpose_f32(const float* w, float* wt, int K, int N, cudaStream_t s) {
+  dim3 grid((N + 31) / 32, (K + 31) / 32), block(32, 8);
+  k_transpose_f32<<<grid, block, 0, s>>>(w, wt, K, N);
+  return cudaGetLastError();
+}
+
+// [images, heads, tokens, 64] -> [images * tokens, heads * 64]
+__global__ void k_hnd_to_token(const float* x, float* y, int images, int heads, int tokens) {
+  const size_t total = static_cast<size_t>(images) * heads * tokens * 64;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int d = static_cast<int>(i % 64);
+    const size_t r = i / 64;
+    const int t = static_cast<int>(r % tokens);
+    const size_t ih = r / tokens;
+    const int h = static_cast<int>(ih % heads);
+    const size_t im = ih / heads;
+    y[(im * tokens + t) * (static_cast<size_t>(heads) * 64) + h * 64 + d] = x[i];
+  }
+}
+cudaError_t hnd_to_token_f32(const float* x, float* y, int images, int heads, int tokens, cudaStream_t s) {
+  const size_t total = static_cast<size_t>(images) * heads * tokens * 64;
+  if (total == 0) return cudaSuccess;
+  k_hnd_to_token<<<ew_grid(total), EW_THREADS, 0, s>>>(x, y, images, heads, tokens);
+  return cudaGetLastError();
+}
+
+}  // namespace vk

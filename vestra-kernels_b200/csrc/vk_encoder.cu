@@ -1,0 +1,389 @@
+// vk_encoder.cu -- the DA3-BASE ViT encoder driver behind vk_encoder_*.
+//
+// The reference crate exposes only operators; Vestra Engine composes them
+// per block (src/lib.rs:52-130 called in the order pre-LN, qkv, rope / qk-norm,
+// attention, out-proj + LayerScale, residual add, LN, fc1 + bias + GELU,
+// fc2 + LayerScale, residual add).  Here one block is seven kernels:
+//
+//   bf16 / Q8_0 math                         residual stream `x` is f32 [M, E]
+//   1. LayerNorm(x)      -> bf16 (or Q8_0) [M, E]
+//   2. QKV GEMM          -> +bias, RoPE on q/k, head-major bf16 q, k, v
+//   3. attention         -> token-major bf16 (or Q8_0) [M, E]
+//   4. out-proj GEMM     -> x += (acc + b) * ls1
+//   5. LayerNorm(x)      -> bf16 (or Q8_0)
+//   6. fc1 GEMM          -> gelu(acc + b) bf16 (or Q8_0) [M, F]
+//   7. fc2 GEMM          -> x += (acc + b) * ls2
+//
+// Images are batched into the GEMMs' M dimension (M = images * tokens).  A
+// forward for a given (images, grid, buffers, stream) is recorded into a CUDA
+// graph on its second call and replayed afterwards.
+#include <stdlib.h>
+
+#include <vector>
+
+#include "vestra_b200.h"
+#include "vk_abi_internal.h"
+#include "vk_internal.h"
+
+using namespace vk;
+
+void host_rotations(const int64_t* pos, size_t n, size_t head_dim, float freq, std::vector<float>& rot);
+int prepare_weight(size_t k, size_t n, const float* w_host, int math, float** w32, __nv_bfloat16** w16, int8_t** wq,
+                   __half** wd, std::vector<void*>* track);
+
+namespace {
+
+struct Acts {
+  __nv_bfloat16 *ln16, *q16, *k16, *v16, *att16, *h16;
+  int8_t *lnq, *attq, *hq;
+  __half *lnd, *attd, *hd;
+  float *ln32, *q32, *k32, *v32, *att32, *tok32, *h32;
+};
+
+void layout_acts(Arena& ar, int math, size_t M, size_t E, size_t F, Acts& a) {
+  a = Acts{};
+  if (math == VK_MATH_F32) {
+    a.ln32 = ar.get<float>(M * E);
+    a.q32 = ar.get<float>(M * E);
+    a.k32 = ar.get<float>(M * E);
+    a.v32 = ar.get<float>(M * E);
+    a.att32 = ar.get<float>(M * E);
+    a.tok32 = ar.get<float>(M * E);
+    a.h32 = ar.get<float>(M * F);
+    return;
+  }
+  a.q16 = ar.get<__nv_bfloat16>(M * E);
+  a.k16 = ar.get<__nv_bfloat16>(M * E);
+  a.v16 = ar.get<__nv_bfloat16>(M * E);
+  if (math == VK_MATH_BF16) {
+    a.ln16 = ar.get<__nv_bfloat16>(M * E);
+    a.att16 = ar.get<__nv_bfloat16>(M * E);
+    a.h16 = ar.get<__nv_bfloat16>(M * F);
+  } else {
+    a.lnq = ar.get<int8_t>(M * E);
+    a.lnd = ar.get<__half>(M * E / 32);
+    a.attq = ar.get<int8_t>(M * E);
+    a.attd = ar.get<__half>(M * E / 32);
+    a.hq = ar.get<int8_t>(M * F);
+    a.hd = ar.get<__half>(M * F / 32);
+  }
+}
+
+int ensure_acts(vk_encoder* enc, size_t M, Acts& a) {
+  const size_t E = enc->embed, F = enc->cfg.ffn;
+  if (M > enc->cap_rows) {
+    if (enc->act) {
+      cudaDeviceSynchronize();
+      cudaFree(enc->act);
+      enc->act = nullptr;
+      enc->cap_rows = 0;
+      for (auto& kv : enc->graphs) cudaGraphExecDestroy(kv.second);
+      enc->graphs.clear();
+      enc->seen.clear();
+    }
+    Arena sizing;
+    layout_acts(sizing, enc->cfg.math, M, E, F, a);
+    VK_TRY_CUDA(cudaMalloc(&enc->act, sizing.off + 256), "encoder activations");
+    enc->cap_rows = M;
+  }
+  Arena ar{enc->act, 0};
+  layout_acts(ar, enc->cfg.math, enc->cap_rows, E, F, a);
+  return VK_OK;
+}
+
+int ensure_rope(vk_encoder* enc, size_t gh, size_t gw) {
+  if (enc->rope && enc->rope_h == gh && enc->rope_w == gw) return VK_OK;
+  const size_t T = gh * gw + 1;
+  std::vector<int64_t> pos(2 * T, 0);
+  for (size_t p = 0; p < gh * gw; ++p) {
+    pos[2 * (p + 1)] = static_cast<int64_t>(p / gw + 1);
+    pos[2 * (p + 1) + 1] = static_cast<int64_t>(p % gw + 1);
+  }
+  std::vector<float> rot;
+  host_rotations(pos.data(), T, 64, enc->cfg.rope_freq, rot);
+  if (enc->rope) {
+    cudaDeviceSynchronize();
+    cudaFree(enc->rope);
+    enc->rope = nullptr;
+    for (auto& kv : enc->graphs) cudaGraphExecDestroy(kv.second);
+    enc->graphs.clear();
+    enc->seen.clear();
+  }
+  VK_TRY_CUDA(cudaMalloc(&enc->rope, rot.size() * sizeof(float)), "rotation table");
+  VK_TRY_CUDA(cudaMemcpy(enc->rope, rot.data(), rot.size() * sizeof(float), cudaMemcpyHostToDevice), "rotation table");
+  enc->rope_h = gh;
+  enc->rope_w = gw;
+  return VK_OK;
+}
+
+// Enqueues one forward on `s`; returns the number of kernels launched or a
+// negative value on a launch error.
+int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const Acts& a, float* x, cudaStream_t s) {
+  const int E = enc->embed, F = enc->cfg.ffn, H = enc->cfg.heads;
+  const int M = static_cast<int>(images * T);
+  const float eps = enc->cfg.eps;
+  const int math = enc->cfg.math;
+  int launches = 0;
+#define VK_L(expr)                         \
+  do {                                     \
+    if ((expr) != cudaSuccess) return -1;  \
+    ++launches;                            \
+  } while (0)
+  for (const EncLayer& L : enc->layers) {
+    GemmEpi qkv;
+    qkv.bias = L.qkv_b;
+    qkv.tokens = static_cast<int>(T);
+    qkv.heads = H;
+    GemmEpi proj;
+    proj.bias = L.proj_b;
+    proj.scale = L.ls1;
+    proj.resid = x;
+    proj.ldo = E;
+    GemmEpi fc1;
+    fc1.bias = L.fc1_b;
+    fc1.ldo = F;
+    GemmEpi fc2;
+    fc2.bias = L.fc2_b;
+    fc2.scale = L.ls2;
+    fc2.resid = x;
+    fc2.ldo = E;
+    if (math == VK_MATH_BF16) {
+      qkv.q = a.q16; qkv.k = a.k16; qkv.v = a.v16; qkv.rope = enc->rope;
+      fc1.out = a.h16;
+      VK_L(layernorm_f32(x, nullptr, a.ln16, nullptr, nullptr, M, E, L.ln1_g, L.ln1_b, eps, s));
+      VK_L(gemm_bf16_tc(a.ln16, L.qkv_w16, M, 3 * E, E, EPI_QKV_BF16, qkv, d_err, s));
+      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)images, H, (int)T, ATTN_OUT_TOKEN_BF16, a.att16, nullptr, s));
+      VK_L(gemm_bf16_tc(a.att16, L.proj_w16, M, E, E, EPI_RESID, proj, d_err, s));
+      VK_L(layernorm_f32(x, nullptr, a.ln16, nullptr, nullptr, M, E, L.ln2_g, L.ln2_b, eps, s));
+      VK_L(gemm_bf16_tc(a.ln16, L.fc1_w16, M, F, E, EPI_BF16_GELU, fc1, d_err, s));
+      VK_L(gemm_bf16_tc(a.h16, L.fc2_w16, M, E, F, EPI_RESID, fc2, d_err, s));
+    } else if (math == VK_MATH_Q8_0) {
+      qkv.q = a.q16; qkv.k = a.k16; qkv.v = a.v16; qkv.rope = enc->rope;
+      fc1.q8 = a.hq;
+      fc1.q8d = a.hd;
+      VK_L(layernorm_f32(x, nullptr, nullptr, a.lnq, a.lnd, M, E, L.ln1_g, L.ln1_b, eps, s));
+      VK_L(gemm_q8_tc(a.lnq, a.lnd, L.qkv_q, L.qkv_d, M, 3 * E, E, EPI_QKV_BF16, qkv, nullptr, d_err, s));
+      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)images, H, (int)T, ATTN_OUT_TOKEN_Q8, a.attq, a.attd, s));
+      VK_L(gemm_q8_tc(a.attq, a.attd, L.proj_q, L.proj_d, M, E, E, EPI_RESID, proj, nullptr, d_err, s));
+      VK_L(layernorm_f32(x, nullptr, nullptr, a.lnq, a.lnd, M, E, L.ln2_g, L.ln2_b, eps, s));
+      VK_L(gemm_q8_tc(a.lnq, a.lnd, L.fc1_q, L.fc1_d, M, F, E, EPI_Q8_GELU, fc1, nullptr, d_err, s));
+      VK_L(gemm_q8_tc(a.hq, a.hd, L.fc2_q, L.fc2_d, M, E, F, EPI_RESID, fc2, nullptr, d_err, s));
+    } else {
+      qkv.q = a.q32; qkv.k = a.k32; qkv.v = a.v32;
+      fc1.out = a.h32;
+      VK_L(layernorm_f32(x, a.ln32, nullptr, nullptr, nullptr, M, E, L.ln1_g, L.ln1_b, eps, s));
+      VK_L(gemm_f32_simt(a.ln32, L.qkv_w32, M, 3 * E, E, EPI_QKV_F32, qkv, s));
+      VK_L(rope2d_f32(a.q32, (int)images * H, (int)T, 64, enc->rope, s));
+      VK_L(rope2d_f32(a.k32, (int)images * H, (int)T, 64, enc->rope, s));
+      VK_L(attention_f32(a.q32, a.k32, a.v32, (int)images * H, (int)T, 64, a.att32, s));
+      VK_L(hnd_to_token_f32(a.att32, a.tok32, (int)images, H, (int)T, s));
+      VK_L(gemm_f32_simt(a.tok32, L.proj_w32, M, E, E, EPI_RESID, proj, s));
+      VK_L(layernorm_f32(x, a.ln32, nullptr, nullptr, nullptr, M, E, L.ln2_g, L.ln2_b, eps, s));
+      VK_L(gemm_f32_simt(a.ln32, L.fc1_w32, M, F, E, EPI_F32_GELU, fc1, s));
+      VK_L(gemm_f32_simt(a.h32, L.fc2_w32, M, E, F, EPI_RESID, fc2, s));
+    }
+  }
+#undef VK_L
+  return launches;
+}
+
+void free_encoder(vk_encoder* enc) {
+  if (!enc) return;
+  cudaSetDevice(enc->device);
+  cudaDeviceSynchronize();
+  for (auto& kv : enc->graphs) cudaGraphExecDestroy(kv.second);
+  for (void* p : enc->allocations) cudaFree(p);
+  if (enc->act) cudaFree(enc->act);
+  if (enc->rope) cudaFree(enc->rope);
+  for (float* p : enc->slots)
+    if (p) cudaFree(p);
+  for (cudaStream_t st : {enc->h2d, enc->d2h, enc->comp})
+    if (st) cudaStreamDestroy(st);
+  delete enc;
+}
+
+}  // namespace
+
+extern "C" int vk_encoder_prepare(vk_ctx* ctx, const vk_encoder_config* cfg, const vk_layer_weights* layers_host,
+                                  vk_encoder** out) {
+  if (!ctx || !cfg || !layers_host || !out) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_prepare: NULL argument");
+  *out = nullptr;
+  cudaSetDevice(ctx->device);
+  if (cfg->layers <= 0 || cfg->heads <= 0 || cfg->ffn <= 0)
+    return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_prepare: empty configuration");
+  const int E = cfg->heads * 64, F = cfg->ffn;
+  if (cfg->math != VK_MATH_F32 && cfg->math != VK_MATH_BF16 && cfg->math != VK_MATH_Q8_0)
+    return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_prepare: unknown math %d", cfg->math);
+  if (cfg->math != VK_MATH_F32 && (E % 128 != 0 || F % 128 != 0 || E > 1024))
+    return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_prepare: tensor-core paths need embed, ffn %% 128 == 0, embed <= 1024");
+  vk_encoder* enc = new vk_encoder();
+  enc->device = ctx->device;
+  enc->cfg = *cfg;
+  enc->embed = E;
+  enc->layers.resize(cfg->layers);
+  auto vec = [&](const float* src, size_t n, float** dst) -> int {
+    if (src == nullptr) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_prepare: NULL layer vector");
+    VK_TRY_CUDA(cudaMalloc(reinterpret_cast<void**>(dst), n * sizeof(float)), "encoder vector");
+    enc->allocations.push_back(*dst);
+    VK_TRY_CUDA(cudaMemcpy(*dst, src, n * sizeof(float), cudaMemcpyHostToDevice), "encoder vector");
+    return VK_OK;
+  };
+  int st = VK_OK;
+  for (int l = 0; l < cfg->layers && st == VK_OK; ++l) {
+    const vk_layer_weights& w = layers_host[l];
+    EncLayer& L = enc->layers[l];
+    L = EncLayer{};
+    if (st == VK_OK) st = vec(w.ln1_gamma, E, &L.ln1_g);
+    if (st == VK_OK) st = vec(w.ln1_beta, E, &L.ln1_b);
+    if (st == VK_OK) st = vec(w.ln2_gamma, E, &L.ln2_g);
+    if (st == VK_OK) st = vec(w.ln2_beta, E, &L.ln2_b);
+    if (st == VK_OK) st = vec(w.qkv_bias, 3 * E, &L.qkv_b);
+    if (st == VK_OK) st = vec(w.proj_bias, E, &L.proj_b);
+    if (st == VK_OK) st = vec(w.ls1, E, &L.ls1);
+    if (st == VK_OK) st = vec(w.fc1_bias, F, &L.fc1_b);
+    if (st == VK_OK) st = vec(w.fc2_bias, E, &L.fc2_b);
+    if (st == VK_OK) st = vec(w.ls2, E, &L.ls2);
+    if (st == VK_OK && (!w.qkv_weight || !w.proj_weight || !w.fc1_weight || !w.fc2_weight))
+      st = vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_prepare: NULL layer weight");
+    if (st == VK_OK)
+      st = prepare_weight(E, 3 * E, w.qkv_weight, cfg->math, &L.qkv_w32, &L.qkv_w16, &L.qkv_q, &L.qkv_d, &enc->allocations);
+    if (st == VK_OK)
+      st = prepare_weight(E, E, w.proj_weight, cfg->math, &L.proj_w32, &L.proj_w16, &L.proj_q, &L.proj_d, &enc->allocations);
+    if (st == VK_OK)
+      st = prepare_weight(E, F, w.fc1_weight, cfg->math, &L.fc1_w32, &L.fc1_w16, &L.fc1_q, &L.fc1_d, &enc->allocations);
+    if (st == VK_OK)
+      st = prepare_weight(F, E, w.fc2_weight, cfg->math, &L.fc2_w32, &L.fc2_w16, &L.fc2_q, &L.fc2_d, &enc->allocations);
+  }
+  if (st != VK_OK) {
+    free_encoder(enc);
+    return st;
+  }
+  *out = enc;
+  return VK_OK;
+}
+
+static int forward_on_stream(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t gh, size_t gw, const float* in,
+                             float* out, cudaStream_t s) {
+  const size_t T = gh * gw + 1, E = enc->embed;
+  const size_t M = images * T;
+  Acts a;
+  VK_TRY(ensure_acts(enc, M, a));
+  VK_TRY(ensure_rope(enc, gh, gw));
+  const auto key = std::make_tuple(images, gh, gw, static_cast<const void*>(in), static_cast<void*>(out), s);
+  const bool use_graph = s != nullptr && getenv("VK_NO_GRAPH") == nullptr;
+  auto it = enc->graphs.find(key);
+  if (use_graph && it != enc->graphs.end()) {
+    VK_TRY_CUDA(cudaGraphLaunch(it->second, s), "encoder graph launch");
+    return VK_OK;
+  }
+  const bool capture = use_graph && enc->seen[key] >= 1;
+  if (capture) VK_TRY_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "encoder capture");
+  if (in != out) {
+    cudaError_t e = cudaMemcpyAsync(out, in, M * E * sizeof(float), cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) {
+      if (capture) {
+        cudaGraph_t g;
+        cudaStreamEndCapture(s, &g);
+      }
+      return vk_cuda_status(e, "encoder input copy");
+    }
+  }
+  const int n = encoder_enqueue(enc, ctx->d_err, images, T, a, out, s);
+  if (capture) {
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (n < 0 || e != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      return vk_fail(VK_ERR_CUDA, "encoder capture failed: %s", cudaGetErrorString(e != cudaSuccess ? e : cudaGetLastError()));
+    }
+    cudaGraphExec_t ex = nullptr;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return vk_cuda_status(e, "encoder graph instantiate");
+    enc->graphs[key] = ex;
+    VK_TRY_CUDA(cudaGraphLaunch(ex, s), "encoder graph launch");
+  } else {
+    if (n < 0) return vk_cuda_status(cudaGetLastError(), "encoder launch");
+    enc->seen[key] += 1;
+  }
+  enc->last_launches = n;
+  return VK_OK;
+}
+
+extern "C" int vk_encoder_forward(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h, size_t grid_w,
+                                  const float* tokens_dev, float* out_dev) {
+  if (!ctx || !enc || !tokens_dev || !out_dev) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_forward: NULL argument");
+  cudaSetDevice(ctx->device);
+  if (images == 0) return VK_OK;
+  if (grid_h == 0 || grid_w == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_forward: empty patch grid");
+  return forward_on_stream(ctx, enc, images, grid_h, grid_w, tokens_dev, out_dev, ctx->stream);
+}
+
+extern "C" int vk_encoder_forward_host(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h, size_t grid_w,
+                                       const float* tokens_host, float* out_host) {
+  if (!ctx || !enc || !tokens_host || !out_host)
+    return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_forward_host: NULL argument");
+  cudaSetDevice(ctx->device);
+  if (images == 0) return VK_OK;
+  if (grid_h == 0 || grid_w == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_forward_host: empty patch grid");
+  const size_t T = grid_h * grid_w + 1, E = enc->embed;
+  size_t chunk = 16;
+  if (const char* c = getenv("VK_E2E_CHUNK")) chunk = static_cast<size_t>(atoi(c));
+  if (chunk == 0 || chunk > images) chunk = images;
+  const size_t rows = chunk * T;
+  if (!enc->comp) {
+    VK_TRY_CUDA(cudaStreamCreateWithFlags(&enc->comp, cudaStreamNonBlocking), "pipeline stream");
+    VK_TRY_CUDA(cudaStreamCreateWithFlags(&enc->h2d, cudaStreamNonBlocking), "pipeline stream");
+    VK_TRY_CUDA(cudaStreamCreateWithFlags(&enc->d2h, cudaStreamNonBlocking), "pipeline stream");
+  }
+  if (rows > enc->slot_rows) {
+    cudaDeviceSynchronize();
+    for (float*& p : enc->slots) {
+      if (p) cudaFree(p);
+      p = nullptr;
+    }
+    for (float*& p : enc->slots) VK_TRY_CUDA(cudaMalloc(&p, rows * E * sizeof(float)), "pipeline slot");
+    enc->slot_rows = rows;
+  }
+  const size_t nchunks = (images + chunk - 1) / chunk;
+  std::vector<cudaEvent_t> ev(3 * nchunks + 1, nullptr);
+  for (auto& e : ev) VK_TRY_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "pipeline event");
+  cudaEvent_t start = ev[3 * nchunks];
+  int st = VK_OK;
+  cudaError_t e = cudaEventRecord(start, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(enc->h2d, start, 0);
+  for (size_t c = 0; c < nchunks && st == VK_OK && e == cudaSuccess; ++c) {
+    const size_t im0 = c * chunk, nim = (images - im0 < chunk) ? images - im0 : chunk;
+    float* slot = enc->slots[c % 3];
+    const size_t bytes = nim * T * E * sizeof(float);
+    cudaEvent_t h2d_done = ev[3 * c], comp_done = ev[3 * c + 1], d2h_done = ev[3 * c + 2];
+    if (c >= 3) e = cudaStreamWaitEvent(enc->h2d, ev[3 * (c - 3) + 2], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(slot, tokens_host + im0 * T * E, bytes, cudaMemcpyHostToDevice, enc->h2d);
+    if (e == cudaSuccess) e = cudaEventRecord(h2d_done, enc->h2d);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(enc->comp, h2d_done, 0);
+    if (e != cudaSuccess) break;
+    st = forward_on_stream(ctx, enc, nim, grid_h, grid_w, slot, slot, enc->comp);
+    if (st != VK_OK) break;
+    e = cudaEventRecord(comp_done, enc->comp);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(enc->d2h, comp_done, 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out_host + im0 * T * E, slot, bytes, cudaMemcpyDeviceToHost, enc->d2h);
+    if (e == cudaSuccess) e = cudaEventRecord(d2h_done, enc->d2h);
+  }
+  if (st == VK_OK && e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, ev[3 * (nchunks - 1) + 2], 0);
+  cudaError_t se = cudaStreamSynchronize(enc->d2h);
+  cudaStreamSynchronize(enc->comp);
+  cudaStreamSynchronize(enc->h2d);
+  for (auto& x : ev) cudaEventDestroy(x);
+  if (st != VK_OK) return st;
+  if (e != cudaSuccess) return vk_cuda_status(e, "vk_encoder_forward_host");
+  if (se != cudaSuccess) return vk_cuda_status(se, "vk_encoder_forward_host");
+  return VK_OK;
+}
+
+extern "C" int vk_encoder_last_launches(const vk_encoder* enc) { return enc ? enc->last_launches : 0; }
+
+extern "C" int vk_encoder_release(vk_encoder* enc) {
+  free_encoder(enc);
+  return VK_OK;
+}

@@ -1,0 +1,272 @@
+// vk_gemm_tc.cu -- bf16 projection GEMM on the 5th-generation tensor cores.
+//
+// Replaces the reference's shape-specialised AVX-512 projections
+// (src/specialized.rs:770-1300: linear_f32_da3_base, linear_bias_scale_f32_da3_base,
+// qkv_f32_da3_base) and the separate bias / GELU / LayerScale / residual passes
+// (src/scalar.rs:65-155, src/dispatch.rs:56-77) with one persistent kernel:
+//
+//   warp 0      TMA producer: A [128 x 64] and W [BN x 64] bf16 tiles, 128B swizzle,
+//               into a STAGES-deep shared-memory ring (mbarrier full/empty pairs)
+//   warp 1      allocates TMEM, one elected lane issues tcgen05.mma (M=128, N=BN,
+//               K=16) into one of two f32 accumulators in TMEM (2 x BN columns)
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (one row per thread),
+//               fused bias / GELU / LayerScale+residual / head-major QKV+RoPE, store
+//
+// The accumulator double buffer lets the epilogue of tile i overlap the MMAs
+// of tile i+1.  Tiles are visited m-major across the persistent grid so the
+// CTAs resident at one time share A row-blocks in L2.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "vk_common.cuh"
+#include "vk_internal.h"
+#include "vk_epilogue.cuh"
+
+namespace vk {
+
+namespace {
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
+constexpr int GEMM_THREADS = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 256;
+};
+}  // namespace
+
+// ------------------------------------------------------------------ kernel
+template <int BN, int MODE>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const GemmEpi epi, int M, int N, int K, int* err) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int n_tiles = N / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kb_n = K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * BM;
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < kb_n; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, err, VK_DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, m0);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, n0);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t aphase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], aphase ^ 1u, err, VK_DEV_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kb_n; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err, VK_DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = smem_desc_k_sw128(smem_u32(sA + stage * C::A_BYTES));
+          const uint64_t bdesc = smem_desc_k_sw128(smem_u32(sB + stage * C::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc + static_cast<uint64_t>(k * 2),
+                     idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32) are this warp's
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t aphase = (it >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], aphase, err, VK_DEV_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const int m0 = (tile / n_tiles) * BM;
+      const int n0 = (tile % n_tiles) * BN;
+      const int row = m0 + quad * 32 + lane;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + static_cast<uint32_t>(c * 32), r);
+        tmem_wait_ld();
+        if (row < M) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          epilogue_chunk<MODE>(epi, row, n0 + c * 32, N, v);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                  uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, int MODE>
+static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmEpi& epi, int M, int N,
+                               int K, int* err, cudaStream_t s) {
+  using C = GemmCfg<BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_bf16<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(C::SMEM));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * (N / BN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  k_gemm_bf16<BN, MODE><<<grid, GEMM_THREADS, C::SMEM, s>>>(ta, tb, epi, M, N, K, err);
+  return cudaGetLastError();
+}
+
+template <int BN>
+static cudaError_t dispatch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, const GemmEpi& epi,
+                                 int M, int N, int K, int* err, cudaStream_t s) {
+  switch (mode) {
+    case EPI_F32: return launch_gemm<BN, EPI_F32>(ta, tb, epi, M, N, K, err, s);
+    case EPI_BF16: return launch_gemm<BN, EPI_BF16>(ta, tb, epi, M, N, K, err, s);
+    case EPI_BF16_GELU: return launch_gemm<BN, EPI_BF16_GELU>(ta, tb, epi, M, N, K, err, s);
+    case EPI_RESID: return launch_gemm<BN, EPI_RESID>(ta, tb, epi, M, N, K, err, s);
+    case EPI_QKV_BF16: return launch_gemm<BN, EPI_QKV_BF16>(ta, tb, epi, M, N, K, err, s);
+    case EPI_QKV_F32: return launch_gemm<BN, EPI_QKV_F32>(ta, tb, epi, M, N, K, err, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t gemm_bf16_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, int M, int N, int K, int mode,
+                         const GemmEpi& epi, int* err, cudaStream_t s) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % BK != 0 || N % 128 != 0) return cudaErrorInvalidValue;
+  if (mode == EPI_RESID && epi.scale == nullptr) return cudaErrorInvalidValue;
+  // Wide tiles when they still give at least one full wave of CTAs.
+  const int m_tiles = (M + BM - 1) / BM;
+  const bool wide = (N % 256 == 0) && m_tiles * (N / 256) >= num_sms();
+  const int bn = wide ? 256 : 128;
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, A, K, M, static_cast<uint64_t>(K) * 2, BK, BM,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, W, K, N, static_cast<uint64_t>(K) * 2, BK, bn,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  return wide ? dispatch_mode<256>(mode, ta, tb, epi, M, N, K, err, s)
+              : dispatch_mode<128>(mode, ta, tb, epi, M, N, K, err, s);
+}
+
+}  // namespace vk
