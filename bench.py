@@ -1,0 +1,334 @@
+"""DA3-BASE ViT encoder images/s on B200 (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl vestra|reference]
+                    [--math bf16|q8|f32] [--images 64] [--grid 24x36]
+
+A step is one 12-layer encoder forward over `--images` synthetic images per
+GPU (random-init weights W~N(0,0.02), b~N(0,0.01), LayerScale 1e-5; tokens
+~N(0,1)), through the C ABI (vk_encoder_forward).  Images are independent, so
+under torchrun every rank runs its own shard (weak scaling, no collective);
+time is the max over ranks of CUDA-event time around K steps.
+
+`e2e` is the same metric through vk_encoder_forward_host: pinned host tokens
+in, host result out, copies pipelined with the compute inside the timed
+region.  `--impl reference` times the reference's CPU fast path (the
+AVX-512 restatement in oracle/, all host cores) on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (ROOT, os.path.join(ROOT, "vestra-kernels_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+
+E, H, F, LAYERS = 768, 12, 3072, 12
+METRIC = "DA3-BASE ViT encoder images/sec @504x336, 1/2/4/8 B200; % of roofline"
+
+
+def gflop_per_image(tokens: int) -> float:
+    """Algorithmic work per image (12 layers): 2*T*E*(3E+E+F+F) for the
+    projections plus 4*H*T^2*64 for attention."""
+    proj = 2.0 * tokens * E * (3 * E + E + F + F)
+    attn = 4.0 * H * tokens * tokens * 64
+    return LAYERS * (proj + attn) / 1e9
+
+
+def make_layers(seed: int = 0):
+    r = np.random.default_rng(seed)
+    f = lambda *s, sc: (r.standard_normal(s, dtype=np.float32) * np.float32(sc))
+    out = []
+    for _ in range(LAYERS):
+        out.append({
+            "ln1_g": np.ones(E, np.float32), "ln1_b": np.zeros(E, np.float32),
+            "qkv_w": f(E, 3 * E, sc=0.02), "qkv_b": f(3 * E, sc=0.01),
+            "proj_w": f(E, E, sc=0.02), "proj_b": f(E, sc=0.01), "ls1": np.full(E, 1e-5, np.float32),
+            "ln2_g": np.ones(E, np.float32), "ln2_b": np.zeros(E, np.float32),
+            "fc1_w": f(E, F, sc=0.02), "fc1_b": f(F, sc=0.01),
+            "fc2_w": f(F, E, sc=0.02), "fc2_b": f(E, sc=0.01), "ls2": np.full(E, 1e-5, np.float32),
+        })
+    return out
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            p = json.load(fh)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16": p["bf16_tflops"], "bf16_sustained": p["bf16_tflops_sustained"],
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU legs
+def cpu_reference_seconds_per_image(grid_h, grid_w, layers, reps: int = 1):
+    """Times the reference's AVX-512 fast path (oracle/vk_cpu_ref.c, all host
+    threads) on one image, 12 layers, `reps` times; returns seconds/image."""
+    from oracle import oracle
+
+    T = grid_h * grid_w + 1
+    x = np.random.default_rng(1).standard_normal((T, E), dtype=np.float32)
+    times = []
+    for _ in range(reps):
+        y = x
+        t0 = time.perf_counter()
+        for layer in layers:
+            y = oracle.cpu_ref_encoder_layer(y, layer, grid_h, grid_w)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times)
+
+
+def traffic_from_profiles():
+    """DRAM bytes per launch of the projection GEMM from the committed ncu
+    summary (profiles/gemm_bf16_encoder64.md, line `traffic_bytes_per_launch:`)."""
+    path = os.path.join(ROOT, "profiles", "gemm_bf16_encoder64.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":")[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    gh, gw = args.grid
+    layers = make_layers(0)
+    cores = os.cpu_count()
+    cpu_reference_seconds_per_image(gh, gw, layers[:1], 1)  # page in
+    for _ in range(args.warmup):
+        cpu_reference_seconds_per_image(gh, gw, layers[:2], 1)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_reference_seconds_per_image(gh, gw, layers, 1)
+    dt = time.perf_counter() - t0
+    value = args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"DA3-BASE 12-layer encoder, 1 image per step @ {gh}x{gw} patches "
+                               f"({gh * gw + 1} tokens), random-init weights", "images_per_step": 1,
+                   "tokens": gh * gw + 1, "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": cores, "kind": "port",
+                         "sample": "1 image x 12 layers per step (reference AVX-512 path restated in C, OpenMP)"},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU leg
+def run_vestra(args, rank, world, local_rank):
+    import torch
+
+    import vestra_kernels as vk
+
+    torch.cuda.set_device(local_rank)
+    math = {"bf16": vk.MATH_BF16, "q8": vk.MATH_Q8_0, "f32": vk.MATH_F32}[args.math]
+    gh, gw = args.grid
+    T = gh * gw + 1
+    B = args.images
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)  # a real stream: the encoder is graph-captured on it
+    ctx = vk.Context(local_rank, stream=stream)
+    enc = vk.Encoder(ctx, make_layers(0), math=math)
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    x = torch.randn(B, T, E, device="cuda", generator=g)
+    out = torch.empty_like(x)
+
+    def step():
+        enc.forward(x, out, B, gh, gw)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    ctx.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local_rank) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        stop.record()
+        barrier()
+    ctx.synchronize()
+    ms = start.elapsed_time(stop)
+    launches = enc.last_launches() * args.steps
+
+    # end to end: pinned host buffers through the C ABI
+    hin = x.cpu().pin_memory()
+    hout = torch.empty_like(hin).pin_memory()
+    for _ in range(2):
+        enc.forward_host(hin, hout, B, gh, gw)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        enc.forward_host(hin, hout, B, gh, gw)
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    # per-kernel device time (eager forward with events between kernels)
+    slots = enc.profile(x, out, B, gh, gw)
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+    if rank != 0:
+        return
+
+    peaks = load_peaks()
+    images = B * world
+    value = images / (ms / 1e3 / args.steps)
+    e2e_value = images / (e2e_ms / 1e3 / args.steps)
+    gf = gflop_per_image(T)
+    # dominant kernel: the projection GEMM (slots 1, 3, 5, 6 of each block)
+    proj_flop = 2.0 * B * T * E * (3 * E + E + F + F) * LAYERS
+    gemm_ms = sum(slots[i] for i in (1, 3, 5, 6)) if math != vk.MATH_F32 else sum(slots[i] for i in (1, 6, 8, 9))
+    attn_ms = slots[2] if math != vk.MATH_F32 else slots[4]
+    gemm_tflops = proj_flop / (gemm_ms / 1e3) / 1e12
+    attn_tflops = (4.0 * H * T * T * 64 * B * LAYERS) / (attn_ms / 1e3) / 1e12
+    peak = peaks["bf16_sustained"]
+    total_ms_eager = sum(slots)
+    line = {
+        "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": {"bf16": "bf16", "q8": "int8", "f32": "f32"}[args.math], "data": "synthetic",
+        "config": {"workload": f"DA3-BASE 12-layer ViT encoder, {B} images/GPU @ {gh * 14}x{gw * 14} "
+                               f"({T} tokens), random-init weights, tokens ~N(0,1)",
+                   "images_per_gpu": B, "global_batch": images, "tokens": T, "layers": LAYERS,
+                   "math": args.math, "parallelism": f"image-sharded x{world}, no collective",
+                   "l2": "inputs larger than L2 (activations 170 MB per step)"},
+        "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": int(hin.numel() * 4),
+                "d2h_bytes_per_step": int(hout.numel() * 4)},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "kernel": "k_gemm_bf16 (projection GEMMs)" if math == vk.MATH_BF16 else
+                     ("k_gemm_q8" if math == vk.MATH_Q8_0 else "k_gemm_f32"),
+                     "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s", "frac": gemm_tflops / peak,
+                     "peak_kind": f"bf16 dense sustained, {peaks['source']}",
+                     "traffic": traffic_from_profiles() if math == vk.MATH_BF16 else None,
+                     "whole_step_tflops": gf * value / world / 1e3,
+                     "whole_step_frac": gf * value / world / 1e3 / peak,
+                     "attention_tflops": attn_tflops,
+                     "kernel_ms": {"layernorm": slots[0] + slots[4] if math != vk.MATH_F32 else slots[0] + slots[7],
+                                   "gemm": gemm_ms, "attention": attn_ms, "eager_total": total_ms_eager}},
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu:
+        s = cpu_reference_seconds_per_image(gh, gw, make_layers(0), reps=1)
+        line["cpu_baseline"] = {"value": 1.0 / s, "unit": "images/s", "cores": os.cpu_count(), "kind": "port",
+                                "sample": "1 image x 12 layers (reference AVX-512 path restated in C, OpenMP)"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="vestra", choices=["vestra", "reference"])
+    ap.add_argument("--math", default="bf16", choices=["bf16", "q8", "f32"])
+    ap.add_argument("--images", type=int, default=64)
+    ap.add_argument("--grid", default="24x36")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.grid = tuple(int(v) for v in args.grid.split("x"))
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch
+
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        run_vestra(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch
+
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -185,6 +185,11 @@ int vk_encoder_forward(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_
  * compute in image chunks (the end-to-end entry point). */
 int vk_encoder_forward_host(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h,
                             size_t grid_w, const float* tokens_host, float* out_host);
+/* One eager forward with CUDA events between kernels: ms_per_slot[i] sums
+ * the device time of the i-th kernel of every block (slots >= 7 for bf16 /
+ * Q8_0, >= 10 for f32; order as in the block description above). */
+int vk_encoder_profile(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h, size_t grid_w,
+                       const float* tokens_dev, float* out_dev, float* ms_per_slot, int slots);
 /* Kernels launched by the last vk_encoder_forward (for accounting). */
 int vk_encoder_last_launches(const vk_encoder* enc);
 int vk_encoder_release(vk_encoder* enc);

@@ -272,3 +272,37 @@ def encoder(x, layers, grid_h, grid_w, heads=12, eps=1e-6, freq=100.0, bf16_poin
     for layer in layers:
         x = encoder_layer(x, layer, grid_h, grid_w, heads, eps, freq, bf16_points)
     return x
+
+
+# ---------------------------------------------------------------- timed CPU baseline
+_REF = None
+
+
+def cpu_ref():
+    """libvk_cpu_ref.so: the AVX-512 + OpenMP restatement of the reference's
+    timed fast path (the CPU baseline bench.py reports)."""
+    global _REF
+    if _REF is None:
+        path = os.path.join(_HERE, "libvk_cpu_ref.so")
+        if not os.path.exists(path):
+            build()
+        _REF = ctypes.CDLL(path)
+    return _REF
+
+
+def cpu_ref_encoder_layer(x, layer: dict, grid_h, grid_w, eps=1e-6, freq=100.0):
+    """One block on the restated AVX-512 path; x [T, 768], modified copy returned."""
+    x = _f32(x).copy()
+    keep = {kk: _f32(layer[kk]) for kk in LAYER_KEYS}
+    st = _Layer(**{kk: _p(vv) for kk, vv in keep.items()})
+    cpu_ref().vkr_encoder_layer(_p(x), _sz(x.shape[0]), _sz(grid_h), _sz(grid_w), ctypes.byref(st),
+                                ctypes.c_float(eps), ctypes.c_float(freq))
+    return x
+
+
+def cpu_ref_flash_attention(q, k, v):
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    heads, n, _ = q.shape
+    out = np.empty_like(q)
+    cpu_ref().vkr_flash_attention(_p(q), _p(k), _p(v), _sz(heads), _sz(n), _p(out))
+    return out

@@ -118,16 +118,18 @@ int ensure_rope(vk_encoder* enc, size_t gh, size_t gw) {
 
 // Enqueues one forward on `s`; returns the number of kernels launched or a
 // negative value on a launch error.
-int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const Acts& a, float* x, cudaStream_t s) {
+int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const Acts& a, float* x, cudaStream_t s,
+                    cudaEvent_t* evs = nullptr) {
   const int E = enc->embed, F = enc->cfg.ffn, H = enc->cfg.heads;
   const int M = static_cast<int>(images * T);
   const float eps = enc->cfg.eps;
   const int math = enc->cfg.math;
   int launches = 0;
-#define VK_L(expr)                         \
-  do {                                     \
-    if ((expr) != cudaSuccess) return -1;  \
-    ++launches;                            \
+#define VK_L(expr)                                      \
+  do {                                                  \
+    if (evs != nullptr) cudaEventRecord(evs[launches], s); \
+    if ((expr) != cudaSuccess) return -1;               \
+    ++launches;                                         \
   } while (0)
   for (const EncLayer& L : enc->layers) {
     GemmEpi qkv;
@@ -184,6 +186,7 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
     }
   }
 #undef VK_L
+  if (evs != nullptr) cudaEventRecord(evs[launches], s);
   return launches;
 }
 
@@ -378,6 +381,39 @@ extern "C" int vk_encoder_forward_host(vk_ctx* ctx, vk_encoder* enc, size_t imag
   if (st != VK_OK) return st;
   if (e != cudaSuccess) return vk_cuda_status(e, "vk_encoder_forward_host");
   if (se != cudaSuccess) return vk_cuda_status(se, "vk_encoder_forward_host");
+  return VK_OK;
+}
+
+extern "C" int vk_encoder_profile(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h, size_t grid_w,
+                                  const float* tokens_dev, float* out_dev, float* ms_per_slot, int slots) {
+  if (!ctx || !enc || !tokens_dev || !out_dev || !ms_per_slot)
+    return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_profile: NULL argument");
+  cudaSetDevice(ctx->device);
+  if (images == 0 || grid_h == 0 || grid_w == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_profile: empty shape");
+  const size_t T = grid_h * grid_w + 1, M = images * T;
+  Acts a;
+  VK_TRY(ensure_acts(enc, M, a));
+  VK_TRY(ensure_rope(enc, grid_h, grid_w));
+  const int per_layer = enc->cfg.math == VK_MATH_F32 ? 10 : 7;
+  if (slots < per_layer) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_profile: need %d slots", per_layer);
+  const int total = per_layer * enc->cfg.layers;
+  std::vector<cudaEvent_t> evs(total + 1);
+  for (auto& e : evs) VK_TRY_CUDA(cudaEventCreate(&e), "profile event");
+  if (tokens_dev != out_dev)
+    VK_TRY_CUDA(cudaMemcpyAsync(out_dev, tokens_dev, M * enc->embed * sizeof(float), cudaMemcpyDeviceToDevice, ctx->stream),
+                "profile input copy");
+  const int n = encoder_enqueue(enc, ctx->d_err, images, T, a, out_dev, ctx->stream, evs.data());
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  for (int i = 0; i < slots; ++i) ms_per_slot[i] = 0.0f;
+  if (n == total && e == cudaSuccess)
+    for (int i = 0; i < n; ++i) {
+      float ms = 0.0f;
+      cudaEventElapsedTime(&ms, evs[i], evs[i + 1]);
+      ms_per_slot[i % per_layer] += ms;
+    }
+  for (auto& ev : evs) cudaEventDestroy(ev);
+  if (e != cudaSuccess) return vk_cuda_status(e, "vk_encoder_profile");
+  if (n != total) return vk_fail(VK_ERR_CUDA, "vk_encoder_profile: launch failed");
   return VK_OK;
 }
 

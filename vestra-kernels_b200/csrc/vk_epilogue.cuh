@@ -1,15 +1,34 @@
 // vk_epilogue.cuh -- the fused GEMM epilogues, applied to 32 consecutive
 // output columns of one row held in registers (one tcgen05.ld of TMEM).
+//
+// epi_math       bias, GELU, LayerScale, RoPE in registers
+// epi_direct     the per-row global store (used where a tile chunk cannot go
+//                through a TMA store: Q8_0 outputs, image boundaries)
+// epilogue_chunk epi_math + epi_direct
 #pragma once
 #include "vk_common.cuh"
 #include "vk_internal.h"
 
 namespace vk {
 
-// ------------------------------------------------------------------ epilogue
-template <int MODE>
-__device__ __forceinline__ void epilogue_chunk(const GemmEpi& p, int row, int col0, int N,
-                                               float (&v)[32]) {
+// Head-major coordinates of a QKV output column chunk.
+struct QkvPos {
+  int g, head, axis, image, t;
+};
+__device__ __forceinline__ QkvPos qkv_pos(const GemmEpi& p, int row, int col0) {
+  QkvPos q;
+  const int E = p.heads * 64;
+  q.g = col0 / E;
+  const int rem = col0 - q.g * E;
+  q.head = rem >> 6;
+  q.axis = (rem >> 5) & 1;
+  q.image = row / p.tokens;
+  q.t = row - q.image * p.tokens;
+  return q;
+}
+
+template <int MODE, bool FAST_GELU = false>
+__device__ __forceinline__ void epi_math(const GemmEpi& p, int row, int col0, float (&v)[32]) {
   if (p.bias != nullptr) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + col0 + j);
@@ -19,42 +38,18 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpi& p, int row, int co
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] *= __ldg(p.scale + col0 + j);
     }
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col0);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-  } else if constexpr (MODE == EPI_BF16 || MODE == EPI_BF16_GELU) {
-    if constexpr (MODE == EPI_BF16_GELU) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-    }
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col0);
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      dst[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
-                          pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
   } else if constexpr (MODE == EPI_RESID) {
-    float4* dst = reinterpret_cast<float4*>(p.resid + row * p.ldo + col0);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float4 r = dst[j];
-      r.x += v[4 * j] * __ldg(p.scale + col0 + 4 * j);
-      r.y += v[4 * j + 1] * __ldg(p.scale + col0 + 4 * j + 1);
-      r.z += v[4 * j + 2] * __ldg(p.scale + col0 + 4 * j + 2);
-      r.w += v[4 * j + 3] * __ldg(p.scale + col0 + 4 * j + 3);
-      dst[j] = r;
-    }
+    for (int j = 0; j < 32; ++j) v[j] *= __ldg(p.scale + col0 + j);
+  } else if constexpr (MODE == EPI_BF16_GELU || MODE == EPI_Q8_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = FAST_GELU ? gelu_erf_fast(v[j]) : gelu_erf(v[j]);
   } else if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32) {
-    const int E = p.heads * 64;
-    const int g = col0 / E;
-    const int rem = col0 - g * E;
-    const int head = rem >> 6;
-    const int axis = (rem >> 5) & 1;
-    const int image = row / p.tokens;
-    const int t = row - image * p.tokens;
-    if (p.rope != nullptr && g < 2) {
+    const QkvPos q = qkv_pos(p, row, col0);
+    if (p.rope != nullptr && q.g < 2) {
       // Axial RoPE, rotate-half pairing (i, i + 16) inside this 32-wide axis
       // half (src/rope.rs:84-93); the chunk is exactly one axis half.
-      const float2* r = reinterpret_cast<const float2*>(p.rope + static_cast<size_t>(t) * 64 + axis * 32);
+      const float2* r = reinterpret_cast<const float2*>(p.rope + static_cast<size_t>(q.t) * 64 + q.axis * 32);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const float2 sc = __ldg(r + i);  // (sin, cos)
@@ -63,28 +58,53 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpi& p, int row, int co
         v[i + 16] = b * sc.y + a * sc.x;
       }
     }
-    const size_t off = ((static_cast<size_t>(image) * p.heads + head) * p.tokens + t) * 64 + axis * 32;
-    void* base = g == 0 ? p.q : (g == 1 ? p.k : p.v);
-    if constexpr (MODE == EPI_QKV_BF16) {
-      uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(base) + off);
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        dst[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
-                            pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
-    } else {
-      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(base) + off);
+  for (int j = 0; j < 4; ++j)
+    d[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                      pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+}
+__device__ __forceinline__ void store_f32x32(float* dst, const float (&v)[32]) {
+  float4* d = reinterpret_cast<float4*>(dst);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  for (int j = 0; j < 8; ++j) d[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+template <int MODE>
+__device__ __forceinline__ void epi_direct(const GemmEpi& p, int row, int col0, int N, float (&v)[32]) {
+  if constexpr (MODE == EPI_F32) {
+    store_f32x32(static_cast<float*>(p.out) + row * p.ldo + col0, v);
+  } else if constexpr (MODE == EPI_BF16 || MODE == EPI_BF16_GELU) {
+    store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col0, v);
+  } else if constexpr (MODE == EPI_RESID) {
+    float4* dst = reinterpret_cast<float4*>(p.resid + row * p.ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 r = dst[j];
+      r.x += v[4 * j];
+      r.y += v[4 * j + 1];
+      r.z += v[4 * j + 2];
+      r.w += v[4 * j + 3];
+      dst[j] = r;
     }
+  } else if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32) {
+    const QkvPos q = qkv_pos(p, row, col0);
+    const size_t off = ((static_cast<size_t>(q.image) * p.heads + q.head) * p.tokens + q.t) * 64 + q.axis * 32;
+    void* base = q.g == 0 ? p.q : (q.g == 1 ? p.k : p.v);
+    if constexpr (MODE == EPI_QKV_BF16)
+      store_bf16x32(static_cast<__nv_bfloat16*>(base) + off, v);
+    else
+      store_f32x32(static_cast<float*>(base) + off, v);
   } else if constexpr (MODE == EPI_Q8_GELU) {
-    // gelu, then this 32-column chunk is exactly one Q8_0 block of the row
+    // this 32-column chunk is exactly one Q8_0 block of the row
     // (quantize_row_q8_0, src/q8_0_dot.rs:34-45).
     float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      v[j] = gelu_erf(v[j]);
-      amax = fmaxf(amax, fabsf(v[j]));
-    }
+    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
     const float dd = amax / 127.0f;
     const float id = dd != 0.0f ? 1.0f / dd : 0.0f;
     p.q8d[static_cast<size_t>(row) * (N / 32) + col0 / 32] = __float2half_rn(dd);
@@ -104,6 +124,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpi& p, int row, int co
     dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
   }
   (void)N;
+}
+
+template <int MODE>
+__device__ __forceinline__ void epilogue_chunk(const GemmEpi& p, int row, int col0, int N, float (&v)[32]) {
+  epi_math<MODE>(p, row, col0, v);
+  epi_direct<MODE>(p, row, col0, N, v);
 }
 
 }  // namespace vk

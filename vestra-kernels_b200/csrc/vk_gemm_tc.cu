@@ -17,6 +17,8 @@
 // CTAs resident at one time share A row-blocks in L2.
 #include <cudaTypedefs.h>
 
+#include <string.h>
+
 #include <mutex>
 
 #include "vk_common.cuh"
@@ -37,21 +39,53 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 256;
+  // epilogue staging: 4 warps x 2 buffers x (32 rows x 128 B)
+  static constexpr int STAGE_OUT_BYTES = 4 * 2 * 4096;
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + STAGE_OUT_BYTES + 256;
 };
+
+// Output element size and the TMA swizzle of the 32 x 32 staging tile.
+template <int MODE>
+struct OutTraits {
+  static constexpr bool F32 = (MODE == EPI_F32 || MODE == EPI_RESID || MODE == EPI_QKV_F32);
+  static constexpr int ROW_BYTES = F32 ? 128 : 64;
+};
+
+// Writes this thread's 32 values as row `lane` of a 32-row staging tile in
+// the TMA 128-byte (f32) or 64-byte (bf16) swizzle, so that the 16-byte
+// chunks of one store instruction spread over all banks.
+template <int MODE>
+__device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const float (&v)[32]) {
+  if constexpr (OutTraits<MODE>::F32) {
+    uint8_t* row = buf + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float4*>(row + ((j ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+    uint8_t* row = buf + lane * 64;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(row + ((j ^ ((lane >> 1) & 3)) << 4)) =
+          make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                     pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+  }
+}
 }  // namespace
 
 // ------------------------------------------------------------------ kernel
 template <int BN, int MODE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const GemmEpi epi, int M, int N, int K, int* err) {
+                const __grid_constant__ CUtensorMap tmO0, const __grid_constant__ CUtensorMap tmO1,
+                const __grid_constant__ CUtensorMap tmO2, const GemmEpi epi, int M, int N, int K, int* err) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* sOut = smem + C::STAGES * C::STAGE_BYTES;  // 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + C::STAGE_OUT_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -147,6 +181,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32) are this warp's
+    uint8_t* stage = sOut + (warp - 2) * 2 * 4096;
+    int sb = 0;
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
@@ -155,23 +191,59 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       const int m0 = (tile / n_tiles) * BM;
       const int n0 = (tile % n_tiles) * BN;
-      const int row = m0 + quad * 32 + lane;
+      const int row0 = m0 + quad * 32;
+      const int row = row0 + lane;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      // A 32-row chunk of the head-major QKV output that crosses an image
+      // boundary (or the end of M) is written row by row instead of by TMA.
+      bool direct = false;
+      int img = 0, t0 = 0;
+      if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32) {
+        img = row0 / epi.tokens;
+        t0 = row0 - img * epi.tokens;
+        direct = (t0 + 32 > epi.tokens) || (row0 + 32 > M);
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tbase + static_cast<uint32_t>(c * 32), r);
         tmem_wait_ld();
-        if (row < M) {
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          epilogue_chunk<MODE>(epi, row, n0 + c * 32, N, v);
+        if (c == BN / 32 - 1) {  // accumulator fully read: hand it back to the MMA warp
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
         }
+        if (row0 >= M) continue;
+        const int col0 = n0 + c * 32;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        epi_math<MODE, true>(epi, row, col0, v);
+        if (direct) {
+          if (row < M) epi_direct<MODE>(epi, row, col0, N, v);
+          continue;
+        }
+        uint8_t* buf = stage + sb * 4096;
+        if (lane == 0) bulk_wait_read<1>();  // the store that last read `buf` is done with it
+        __syncwarp();
+        stage_row<MODE>(buf, lane, v);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (MODE == EPI_RESID) {
+            tma_reduce_add_2d(&tmO0, buf, col0, row0);
+          } else if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32) {
+            const QkvPos q = qkv_pos(epi, row0, col0);
+            const CUtensorMap* map = q.g == 0 ? &tmO0 : (q.g == 1 ? &tmO1 : &tmO2);
+            tma_store_3d(map, buf, q.axis * 32, t0, img * epi.heads + q.head);
+          } else {
+            tma_store_2d(&tmO0, buf, col0, row0);
+          }
+          bulk_commit();
+        }
+        sb ^= 1;
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait<0>();
   }
   __syncthreads();
   if (warp == 1) {
@@ -208,6 +280,20 @@ bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
   return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                  uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
+                  CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {box0, box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -219,9 +305,13 @@ int num_sms() {
   return n;
 }
 
+struct OutMaps {
+  CUtensorMap m[3];
+};
+
 template <int BN, int MODE>
-static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmEpi& epi, int M, int N,
-                               int K, int* err, cudaStream_t s) {
+static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om, const GemmEpi& epi,
+                               int M, int N, int K, int* err, cudaStream_t s) {
   using C = GemmCfg<BN>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -232,20 +322,20 @@ static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, con
   }
   const int tiles = ((M + BM - 1) / BM) * (N / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  k_gemm_bf16<BN, MODE><<<grid, GEMM_THREADS, C::SMEM, s>>>(ta, tb, epi, M, N, K, err);
+  k_gemm_bf16<BN, MODE><<<grid, GEMM_THREADS, C::SMEM, s>>>(ta, tb, om.m[0], om.m[1], om.m[2], epi, M, N, K, err);
   return cudaGetLastError();
 }
 
 template <int BN>
-static cudaError_t dispatch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, const GemmEpi& epi,
-                                 int M, int N, int K, int* err, cudaStream_t s) {
+static cudaError_t dispatch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om,
+                                 const GemmEpi& epi, int M, int N, int K, int* err, cudaStream_t s) {
   switch (mode) {
-    case EPI_F32: return launch_gemm<BN, EPI_F32>(ta, tb, epi, M, N, K, err, s);
-    case EPI_BF16: return launch_gemm<BN, EPI_BF16>(ta, tb, epi, M, N, K, err, s);
-    case EPI_BF16_GELU: return launch_gemm<BN, EPI_BF16_GELU>(ta, tb, epi, M, N, K, err, s);
-    case EPI_RESID: return launch_gemm<BN, EPI_RESID>(ta, tb, epi, M, N, K, err, s);
-    case EPI_QKV_BF16: return launch_gemm<BN, EPI_QKV_BF16>(ta, tb, epi, M, N, K, err, s);
-    case EPI_QKV_F32: return launch_gemm<BN, EPI_QKV_F32>(ta, tb, epi, M, N, K, err, s);
+    case EPI_F32: return launch_gemm<BN, EPI_F32>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_BF16: return launch_gemm<BN, EPI_BF16>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_BF16_GELU: return launch_gemm<BN, EPI_BF16_GELU>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_RESID: return launch_gemm<BN, EPI_RESID>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_QKV_BF16: return launch_gemm<BN, EPI_QKV_BF16>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_QKV_F32: return launch_gemm<BN, EPI_QKV_F32>(ta, tb, om, epi, M, N, K, err, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -265,8 +355,28 @@ cudaError_t gemm_bf16_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, int M, 
   if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, W, K, N, static_cast<uint64_t>(K) * 2, BK, bn,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  return wide ? dispatch_mode<256>(mode, ta, tb, epi, M, N, K, err, s)
-              : dispatch_mode<128>(mode, ta, tb, epi, M, N, K, err, s);
+  OutMaps om;
+  memset(&om, 0, sizeof(om));
+  bool ok = true;
+  const bool f32 = (mode == EPI_F32 || mode == EPI_RESID || mode == EPI_QKV_F32);
+  const CUtensorMapDataType odt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t esz = f32 ? 4 : 2;
+  const CUtensorMapSwizzle oswz = f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (mode == EPI_QKV_BF16 || mode == EPI_QKV_F32) {
+    if (epi.tokens <= 0 || M % epi.tokens != 0 || N != 3 * epi.heads * 64) return cudaErrorInvalidValue;
+    const uint64_t images = M / epi.tokens;
+    void* bases[3] = {epi.q, epi.k, epi.v};
+    for (int g = 0; g < 3 && ok; ++g)
+      ok = make_tmap_3d(&om.m[g], odt, bases[g], 64, epi.tokens, images * epi.heads, 64 * esz,
+                        static_cast<uint64_t>(epi.tokens) * 64 * esz, 32, 32, oswz);
+  } else if (mode == EPI_RESID) {
+    ok = make_tmap_2d(&om.m[0], odt, epi.resid, N, M, static_cast<uint64_t>(epi.ldo) * esz, 32, 32, oswz);
+  } else {
+    ok = make_tmap_2d(&om.m[0], odt, epi.out, N, M, static_cast<uint64_t>(epi.ldo) * esz, 32, 32, oswz);
+  }
+  if (!ok) return cudaErrorInvalidValue;
+  return wide ? dispatch_mode<256>(mode, ta, tb, om, epi, M, N, K, err, s)
+              : dispatch_mode<128>(mode, ta, tb, om, epi, M, N, K, err, s);
 }
 
 }  // namespace vk

@@ -45,6 +45,10 @@ bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
                   uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                   uint32_t box_outer, CUtensorMapSwizzle swz);
 
+bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+                  uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                  uint32_t box1, CUtensorMapSwizzle swz);
+
 int num_sms();
 
 // bf16 x bf16 -> f32 tcgen05 GEMM: C[M,N] = A[M,K] . W[N,K]^T (both K-major),

@@ -71,6 +71,7 @@ SIGNATURES = {
     "vk_encoder_prepare": (_I, [_P, _P, _P, ctypes.POINTER(_P)]),
     "vk_encoder_forward": (_I, [_P, _P, _S, _S, _S, _P, _P]),
     "vk_encoder_forward_host": (_I, [_P, _P, _S, _S, _S, _P, _P]),
+    "vk_encoder_profile": (_I, [_P, _P, _S, _S, _S, _P, _P, _P, _I]),
     "vk_encoder_last_launches": (_I, [_P]),
     "vk_encoder_release": (_I, [_P]),
 }
@@ -358,6 +359,7 @@ class Encoder:
         import numpy as np
 
         self.ctx = ctx
+        self.math = math
         self.embed = heads * 64
         keep, structs = [], (_LayerWeights * len(layers))()
         for i, layer in enumerate(layers):
@@ -380,6 +382,14 @@ class Encoder:
         """Host tensors (pinned for overlap); copies are pipelined with compute."""
         _check(lib().vk_encoder_forward_host(self.ctx.handle, self.handle, images, grid_h, grid_w,
                                              ctypes.c_void_p(tokens.data_ptr()), ctypes.c_void_p(out.data_ptr())))
+
+    def profile(self, tokens, out, images: int, grid_h: int, grid_w: int):
+        """Per-kernel device ms of one eager forward, summed over blocks."""
+        ms = (ctypes.c_float * 16)()
+        _check(lib().vk_encoder_profile(self.ctx.handle, self.handle, images, grid_h, grid_w, _ptr(tokens),
+                                        _ptr(out), ms, 16))
+        n = 10 if self.math == MATH_F32 else 7
+        return [float(ms[i]) for i in range(n)]
 
     def last_launches(self) -> int:
         return int(lib().vk_encoder_last_launches(self.handle))
