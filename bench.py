@@ -299,7 +299,7 @@ def run_vestra(args, rank, world, local_rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="vestra", choices=["vestra", "reference"])
     ap.add_argument("--math", default="bf16", choices=["bf16", "q8", "f32"])
