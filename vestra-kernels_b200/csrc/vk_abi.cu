@@ -274,7 +274,7 @@ static int attention64(vk_ctx* ctx, const float* q, const float* k, const float*
   VK_TRY_CUDA(cast_f32_bf16(q, q16, n, s), name);
   VK_TRY_CUDA(cast_f32_bf16(k, k16, n, s), name);
   VK_TRY_CUDA(cast_f32_bf16(v, v16, n, s), name);
-  return vk_cuda_status(attention_bf16(q16, k16, v16, 1, (int)heads, (int)tokens, ATTN_OUT_HEAD_F32, out, nullptr, s), name);
+  return vk_cuda_status(attention_bf16(q16, k16, v16, 1, (int)heads, (int)tokens, ATTN_OUT_HEAD_F32, out, nullptr, ctx->d_err, s), name);
 }
 
 extern "C" int vk_flash_attention_f32_da3_base(vk_ctx* ctx, const float* query, const float* key, const float* value,

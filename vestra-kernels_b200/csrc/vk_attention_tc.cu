@@ -1,0 +1,309 @@
+// vk_attention_tc.cu -- bf16 flash attention on the 5th-generation tensor
+// cores for [images * heads, tokens, 64] head-major Q, K, V.
+//
+// Replaces flash_attention_f32_da3_base / attention::attention on the bf16
+// path (src/specialized.rs:730-765, 1400-1562; src/attention.rs:111-201):
+// non-causal softmax(Q K^T / 8) V with an online softmax over key blocks.
+//
+// One CTA = one (image, head) and 128 queries; 2 CTAs per SM share the SM
+// (256 TMEM columns each) so one CTA's softmax overlaps the other's MMAs.
+//
+//   warp 0      TMA: Q tile once, then K and V blocks of 128 keys (2 stages)
+//   warp 1      TMEM owner; one lane issues
+//                 S(j) = Q K_j^T        (M=128, N=128, K=64; A, B from smem)
+//                 O(j) = P(j) V_j        (M=128, N=64, K=128; A = P from TMEM)
+//   warps 2..5  one query row per thread: read S(j) from TMEM, running max,
+//               p = 2^(s*log2e/8 - m), row sum, P(j) -> TMEM as bf16; fold
+//               O(j-1) into f32 registers with the max correction; finally
+//               normalise and store token-major bf16 / Q8_0 or head-major f32.
+// TMEM: S at columns [0,128), P at [128,192) (bf16 pairs), O at [192,256).
+#include "vk_common.cuh"
+#include "vk_internal.h"
+
+namespace vk {
+
+namespace {
+constexpr int AQ = 128;       // queries per CTA
+constexpr int AKV = 128;      // keys per block
+constexpr int AST = 2;        // K/V pipeline stages
+constexpr int A_THREADS = 192;
+constexpr int TILE_BYTES = 128 * 128;  // 128 rows x 64 bf16
+constexpr uint32_t COL_S = 0, COL_P = 128, COL_O = 192;
+constexpr size_t ATT_SMEM = 1024 + TILE_BYTES * (1 + 2 * AST) + 256;
+}  // namespace
+
+template <int OUT>
+__global__ void __launch_bounds__(A_THREADS, 2)
+    k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, int heads, int tokens, void* out, __half* out_q8d,
+                   int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + TILE_BYTES;
+  uint8_t* sV = sK + AST * TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + AST * TILE_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + AST;
+  uint64_t* s_full = kv_empty + AST;
+  uint64_t* s_empty = s_full + 1;
+  uint64_t* p_full = s_empty + 1;
+  uint64_t* o_full = p_full + 1;
+  uint64_t* o_empty = o_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int q0 = blockIdx.x * AQ;
+  const int nb = (tokens + AKV - 1) / AKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < AST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 128);
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+    mbar_init(o_empty, 128);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_3d(sQ, &tmQ, q_full, 0, q0, bh);
+      for (int j = 0; j < nb; ++j) {
+        const int st = j % AST;
+        if (!mbar_wait(&kv_empty[st], ((j / AST) & 1) ^ 1, err, VK_DEV_TIMEOUT_PRODUCER)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        tma_load_3d(sK + st * TILE_BYTES, &tmK, &kv_full[st], 0, j * AKV, bh);
+        tma_load_3d(sV + st * TILE_BYTES, &tmV, &kv_full[st], 0, j * AKV, bh);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(128, 128);
+      constexpr uint32_t idO = idesc_bf16_bmn(128, 64);
+      bool ok = mbar_wait(q_full, 0, err, VK_DEV_TIMEOUT_MMA);
+      const uint64_t qdesc = smem_desc_k_sw128(smem_u32(sQ));
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % AST;
+        if (!mbar_wait(&kv_full[st], (j / AST) & 1, err, VK_DEV_TIMEOUT_MMA)) return false;
+        if (j > 0 && !mbar_wait(s_empty, (j - 1) & 1, err, VK_DEV_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint64_t kdesc = smem_desc_k_sw128(smem_u32(sK + st * TILE_BYTES));
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_f16(tmem + COL_S, qdesc + static_cast<uint64_t>(k * 2), kdesc + static_cast<uint64_t>(k * 2), idS,
+                   k > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < nb && ok; ++j) {
+        if (j + 1 < nb && !issue_s(j + 1)) break;
+        if (!mbar_wait(p_full, j & 1, err, VK_DEV_TIMEOUT_MMA)) break;
+        if (!mbar_wait(o_empty, (j & 1) ^ 1, err, VK_DEV_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const int st = j % AST;
+        const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(sV + st * TILE_BYTES));
+#pragma unroll
+        for (int k = 0; k < AKV / 16; ++k)
+          umma_f16_ts(tmem + COL_O, tmem + COL_P + static_cast<uint32_t>(k * 8),
+                      vdesc + static_cast<uint64_t>(k * (2048 >> 4)), idO, k > 0 ? 1u : 0u);
+        umma_commit(o_full);
+        umma_commit(&kv_empty[st]);
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const int qrow = q0 + quad * 32 + lane;
+    const float sl2 = 0.125f * 1.4426950408889634f;  // (1/sqrt(64)) * log2(e)
+    float o[64];
+#pragma unroll
+    for (int d = 0; d < 64; ++d) o[d] = 0.0f;
+    float m_run = -INFINITY;  // running max of s * sl2
+    float m_o = -INFINITY;    // normalisation of o[]
+    float l_run = 0.0f;
+    bool ok = true;
+    float m_prev = -INFINITY;  // max after the previous block (normalisation of O(j-1))
+    for (int j = 0; j < nb && ok; ++j) {
+      if (!mbar_wait(s_full, j & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int kbase = j * AKV;
+      const int valid = tokens - kbase;  // keys of this block that exist (may exceed 128)
+      // pass 1: block max
+      float bmax = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + COL_S + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c * 32 + i < valid) bmax = fmaxf(bmax, __uint_as_float(r[i]));
+      }
+      const float m_new = fmaxf(m_run, bmax * sl2);
+      // fold the previous block's output while the tensor core computes
+      if (j > 0) {
+        uint32_t r0[32], r1[32];
+        if (!mbar_wait(o_full, (j - 1) & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float f = (m_o == -INFINITY) ? 0.0f : ex2_approx(m_o - m_prev);
+        tmem_ld32(tmem + lane_base + COL_O, r0);
+        tmem_wait_ld();
+#pragma unroll
+        for (int d = 0; d < 32; ++d) o[d] = o[d] * f + __uint_as_float(r0[d]);
+        tmem_ld32(tmem + lane_base + COL_O + 32, r1);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(o_empty);
+#pragma unroll
+        for (int d = 0; d < 32; ++d) o[32 + d] = o[32 + d] * f + __uint_as_float(r1[d]);
+        m_o = m_prev;
+      }
+      // pass 2: probabilities -> P (bf16 pairs) in TMEM, row sum
+      float bsum = 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + COL_S + c * 32, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int k0 = c * 32 + 2 * i;
+          const float p0 = k0 < valid ? ex2_approx(fmaf(__uint_as_float(r[2 * i]), sl2, -m_new)) : 0.0f;
+          const float p1 = k0 + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), sl2, -m_new)) : 0.0f;
+          bsum += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(tmem + lane_base + COL_P + c * 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(s_empty);
+      mbar_arrive(p_full);
+      l_run = l_run * ((m_run == -INFINITY) ? 0.0f : ex2_approx(m_run - m_new)) + bsum;
+      m_prev = m_new;
+      m_run = m_new;
+    }
+    if (ok && mbar_wait(o_full, (nb - 1) & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+      // o is normalised to m_o, the last block's O to m_run
+      tc_fence_after();
+      uint32_t r0[32];
+      const float f = (m_o == -INFINITY) ? 0.0f : ex2_approx(m_o - m_run);
+      const float inv = 1.0f / l_run;
+      tmem_ld32(tmem + lane_base + COL_O, r0);
+      tmem_wait_ld();
+#pragma unroll
+      for (int d = 0; d < 32; ++d) o[d] = (o[d] * f + __uint_as_float(r0[d])) * inv;
+      tmem_ld32(tmem + lane_base + COL_O + 32, r0);
+      tmem_wait_ld();
+#pragma unroll
+      for (int d = 0; d < 32; ++d) o[32 + d] = (o[32 + d] * f + __uint_as_float(r0[d])) * inv;
+      if (qrow < tokens) {
+        const int b_img = bh / heads, h = bh - b_img * heads;
+        if constexpr (OUT == ATTN_OUT_HEAD_F32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + (static_cast<size_t>(bh) * tokens + qrow) * 64);
+#pragma unroll
+          for (int d = 0; d < 16; ++d) dst[d] = make_float4(o[4 * d], o[4 * d + 1], o[4 * d + 2], o[4 * d + 3]);
+        } else if constexpr (OUT == ATTN_OUT_TOKEN_BF16) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) +
+                                                (static_cast<size_t>(b_img) * tokens + qrow) * (heads * 64) + h * 64);
+#pragma unroll
+          for (int d = 0; d < 8; ++d)
+            dst[d] = make_uint4(pack_bf16x2(o[8 * d], o[8 * d + 1]), pack_bf16x2(o[8 * d + 2], o[8 * d + 3]),
+                                pack_bf16x2(o[8 * d + 4], o[8 * d + 5]), pack_bf16x2(o[8 * d + 6], o[8 * d + 7]));
+        } else {
+          const size_t row = static_cast<size_t>(b_img) * tokens + qrow;
+          int8_t* dst = static_cast<int8_t*>(out) + row * (heads * 64) + h * 64;
+#pragma unroll
+          for (int blk = 0; blk < 2; ++blk) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int d = 0; d < 32; ++d) amax = fmaxf(amax, fabsf(o[blk * 32 + d]));
+            const float dd = amax / 127.0f;
+            const float id = dd != 0.0f ? 1.0f / dd : 0.0f;
+            uint32_t w[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              uint32_t packed = 0;
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const float qf = fminf(fmaxf(roundf(o[blk * 32 + 4 * q + t] * id), -127.0f), 127.0f);
+                packed |= (static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xffu) << (8 * t);
+              }
+              w[q] = packed;
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(dst + blk * 32);
+            d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            out_q8d[row * (heads * 2) + h * 2 + blk] = __float2half_rn(dd);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+template <int OUT>
+static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int images,
+                               int heads, int tokens, void* out, __half* q8d, int* err, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_attention_tc<OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(ATT_SMEM));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  dim3 grid((tokens + AQ - 1) / AQ, images * heads);
+  k_attention_tc<OUT><<<grid, A_THREADS, ATT_SMEM, s>>>(mq, mk, mv, heads, tokens, out, q8d, err);
+  return cudaGetLastError();
+}
+
+cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int images,
+                           int heads, int tokens, int out_mode, void* out, __half* out_q8d, int* err,
+                           cudaStream_t s) {
+  if (images <= 0 || heads <= 0 || tokens <= 0) return cudaErrorInvalidValue;
+  CUtensorMap mq, mk, mv;
+  const uint64_t bh = static_cast<uint64_t>(images) * heads;
+  const void* bases[3] = {q, k, v};
+  CUtensorMap* maps[3] = {&mq, &mk, &mv};
+  for (int i = 0; i < 3; ++i)
+    if (!make_tmap_3d(maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, bases[i], 64, tokens, bh, 128,
+                      static_cast<uint64_t>(tokens) * 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  switch (out_mode) {
+    case ATTN_OUT_HEAD_F32: return launch_attn<ATTN_OUT_HEAD_F32>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
+    case ATTN_OUT_TOKEN_BF16: return launch_attn<ATTN_OUT_TOKEN_BF16>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
+    case ATTN_OUT_TOKEN_Q8: return launch_attn<ATTN_OUT_TOKEN_Q8>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace vk

@@ -218,10 +218,26 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
   return d;
 }
 
+// MN-major operand tile (rows along K, 128-byte rows along M/N) written by
+// TMA with the 128-byte swizzle: 8-row groups along K are 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;              // LBO (one 64-element atom along N)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;      // SBO: next 8 rows along K
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
 // Instruction descriptor: kind::f16 with bf16 A/B, f32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
+}
+// As idesc_bf16 with B MN-major (B rows run along K).
+__host__ __device__ constexpr uint32_t idesc_bf16_bmn(int M, int N) {
+  return idesc_bf16(M, N) | (1u << 16);
 }
 // Instruction descriptor: kind::i8 with signed A/B, s32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_s8(int M, int N) {
@@ -261,8 +277,23 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+// 32 lanes x 16 columns store from registers into TMEM.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // A&S 7.1.26 erf and the exact-erf GELU of the reference (0.5 x (1 + erf(x/sqrt 2))).

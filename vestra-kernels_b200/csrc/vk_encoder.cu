@@ -154,7 +154,7 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
       fc1.out = a.h16;
       VK_L(layernorm_f32(x, nullptr, a.ln16, nullptr, nullptr, M, E, L.ln1_g, L.ln1_b, eps, s));
       VK_L(gemm_bf16_tc(a.ln16, L.qkv_w16, M, 3 * E, E, EPI_QKV_BF16, qkv, d_err, s));
-      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)images, H, (int)T, ATTN_OUT_TOKEN_BF16, a.att16, nullptr, s));
+      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)images, H, (int)T, ATTN_OUT_TOKEN_BF16, a.att16, nullptr, d_err, s));
       VK_L(gemm_bf16_tc(a.att16, L.proj_w16, M, E, E, EPI_RESID, proj, d_err, s));
       VK_L(layernorm_f32(x, nullptr, a.ln16, nullptr, nullptr, M, E, L.ln2_g, L.ln2_b, eps, s));
       VK_L(gemm_bf16_tc(a.ln16, L.fc1_w16, M, F, E, EPI_BF16_GELU, fc1, d_err, s));
@@ -165,7 +165,7 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
       fc1.q8d = a.hd;
       VK_L(layernorm_f32(x, nullptr, nullptr, a.lnq, a.lnd, M, E, L.ln1_g, L.ln1_b, eps, s));
       VK_L(gemm_q8_tc(a.lnq, a.lnd, L.qkv_q, L.qkv_d, M, 3 * E, E, EPI_QKV_BF16, qkv, nullptr, d_err, s));
-      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)images, H, (int)T, ATTN_OUT_TOKEN_Q8, a.attq, a.attd, s));
+      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)images, H, (int)T, ATTN_OUT_TOKEN_Q8, a.attq, a.attd, d_err, s));
       VK_L(gemm_q8_tc(a.attq, a.attd, L.proj_q, L.proj_d, M, E, E, EPI_RESID, proj, nullptr, d_err, s));
       VK_L(layernorm_f32(x, nullptr, nullptr, a.lnq, a.lnd, M, E, L.ln2_g, L.ln2_b, eps, s));
       VK_L(gemm_q8_tc(a.lnq, a.lnd, L.fc1_q, L.fc1_d, M, F, E, EPI_Q8_GELU, fc1, nullptr, d_err, s));
