@@ -133,6 +133,18 @@ int vk_gemm_q8_0(vk_ctx* ctx, size_t m, size_t n, size_t k, const vk_block_q8_0*
 int vk_gemm_q8_0_block_dots(vk_ctx* ctx, size_t m, size_t n, size_t k,
                             const vk_block_q8_0* a_q, const vk_block_q8_0* b_q, int32_t* dots);
 
+/* vk_gemm_q8_0 for callers that cannot allocate device memory (hosts whose
+ * device memory is budgeted up front, plugins inside an engine that owns
+ * every allocation).  It has no counterpart in the reference.  It takes no
+ * context and unpacks the blocks into a fixed 8 MiB array inside the library
+ * instead of a cudaMalloc'd workspace: (m + n) * k + (m + n) * (k / 32) * 2
+ * bytes must fit (VK_UNSUPPORTED_SHAPE otherwise).  The first call on a
+ * device looks the array up and should come before any stream capture; calls
+ * that overlap on the GPU share the array and race.  `stream` is a
+ * cudaStream_t (NULL = legacy default stream); a_q, b_q, c as in vk_gemm_q8_0. */
+int vk_gemm_q8_0_noalloc(void* stream, size_t m, size_t n, size_t k, const vk_block_q8_0* a_q,
+                         const vk_block_q8_0* b_q, float* c);
+
 /* --------------------------------------------------------- prepared values
  * Mirrors the prepared-value objects of the reference (CudaLinearF32,
  * src/cuda.rs:1233-1334): weights are converted and laid out once. */

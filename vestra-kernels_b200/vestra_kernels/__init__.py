@@ -64,6 +64,7 @@ SIGNATURES = {
     "vk_quantize_row_q8_0": (_I, [_P, _P, _S, _P]),
     "vk_gemm_q8_0": (_I, [_P, _S, _S, _S, _P, _P, _P]),
     "vk_gemm_q8_0_block_dots": (_I, [_P, _S, _S, _S, _P, _P, _P]),
+    "vk_gemm_q8_0_noalloc": (_I, [_P, _S, _S, _S, _P, _P, _P]),
     "vk_prepare_linear": (_I, [_P, _S, _S, _P, _P, _P, _I, ctypes.POINTER(_P)]),
     "vk_prepare_linear_q8_0": (_I, [_P, _S, _S, _P, _P, _P, ctypes.POINTER(_P)]),
     "vk_linear_run": (_I, [_P, _P, _S, _P, _P]),
