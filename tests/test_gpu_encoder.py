@@ -128,3 +128,17 @@ def test_graph_replay_and_host_path_match(vk, ctx, oracle_lib):
             assert np.array_equal(hout.numpy(), outs[0])
     finally:
         del os.environ["VK_E2E_CHUNK"]
+
+
+def test_large_batch_matches_single_images(vk, ctx, oracle_lib):
+    """16 images (every GEMM on the CTA-pair kernel) against the same images
+    run alone (single-CTA kernels)."""
+    gh, gw = 24, 36
+    T = gh * gw + 1
+    layers = make_layers(1, 15, ls=1.0)
+    x = np.random.default_rng(16).standard_normal((16, T, E)).astype(np.float32)
+    big, _ = run_encoder(vk, ctx, layers, x, 16, gh, gw, vk.MATH_BF16)
+    for i in (0, 7, 15):
+        one, _ = run_encoder(vk, ctx, layers, x[i:i + 1].copy(), 1, gh, gw, vk.MATH_BF16)
+        err = rel_l2(big[i] - x[i], one[0] - x[i])
+        assert err < 1e-3, (i, err)

@@ -283,3 +283,34 @@ def test_gelu_add_bias_layerscale(vk, ctx, oracle_lib):
     d = dev(np.array([1.0, -2.0, 3.5], np.float32))
     vk.add(d, dev(np.array([0.5, 2.0, -1.0], np.float32)), ctx=ctx)
     assert host(d).tolist() == [1.5, 0.0, 2.5]
+
+
+@pytest.mark.parametrize("k,n", SHAPES)
+def test_linear_bf16_pair_kernel_large_m(vk, ctx, k, n):
+    """M large enough for the CTA-pair (256 x 256) kernel; torch fp32 matmul
+    of the same bf16-rounded operands as reference (TF32 off)."""
+    ctx.set_math(vk.MATH_BF16)
+    try:
+        m = 4096 + 37
+        g = torch.Generator(device="cuda").manual_seed(n + k)
+        x = torch.randn(m, k, device="cuda", generator=g)
+        w = torch.randn(k, n, device="cuda", generator=g) * 0.02
+        b = torch.randn(n, device="cuda", generator=g) * 0.01
+        s = torch.randn(n, device="cuda", generator=g)
+        out = torch.empty(m * n, device="cuda")
+        torch.cuda.synchronize()  # ctx runs on its own stream
+        assert vk.linear_f32_da3_base(m, n, k, x, w, out, ctx=ctx)
+        ctx.synchronize()
+        torch.backends.cuda.matmul.allow_tf32 = False
+        ref = x.bfloat16().float() @ w.bfloat16().float()
+        err = (out.view(m, n) - ref).norm() / ref.norm()
+        assert float(err) < 1e-5, float(err)
+        if n == 768:
+            out2 = torch.empty(m * n, device="cuda")
+            torch.cuda.synchronize()
+            assert vk.linear_bias_scale_f32_da3_base(m, n, k, x, w, b, s, out2, ctx=ctx)
+            ctx.synchronize()
+            ref2 = (ref + b) * s
+            assert float((out2.view(m, n) - ref2).norm() / ref2.norm()) < 1e-5
+    finally:
+        ctx.set_math(vk.MATH_F32)
