@@ -285,6 +285,10 @@ def run_vestra(args, rank, world, local_rank):
                      "whole_step_tflops": gf * value / world / 1e3,
                      "whole_step_frac": gf * value / world / 1e3 / peak,
                      "attention_tflops": attn_tflops,
+                     "slot_ms": dict(zip(["ln1", "qkv", "attention", "proj", "ln2", "fc1", "fc2"]
+                                         if math != vk.MATH_F32 else
+                                         ["ln1", "qkv", "rope_q", "rope_k", "attention", "to_tokens", "proj",
+                                          "ln2", "fc1", "fc2"], [round(x, 4) for x in slots])),
                      "kernel_ms": {"layernorm": slots[0] + slots[4] if math != vk.MATH_F32 else slots[0] + slots[7],
                                    "gemm": gemm_ms, "attention": attn_ms, "eager_total": total_ms_eager}},
         "clocks": clk.summary(),

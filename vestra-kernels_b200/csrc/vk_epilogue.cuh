@@ -27,20 +27,32 @@ __device__ __forceinline__ QkvPos qkv_pos(const GemmEpi& p, int row, int col0) {
   return q;
 }
 
+// bias32 / scale32 point at the 32 bias / scale values of this chunk
+// (16-byte aligned, global or shared memory) or are null.
 template <int MODE, bool FAST_GELU = false>
-__device__ __forceinline__ void epi_math(const GemmEpi& p, int row, int col0, float (&v)[32]) {
-  if (p.bias != nullptr) {
+__device__ __forceinline__ void epi_math(const GemmEpi& p, int row, int col0, float (&v)[32], const float* bias32,
+                                         const float* scale32) {
+  if (bias32 != nullptr) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + col0 + j);
-  }
-  if constexpr (MODE == EPI_F32) {
-    if (p.scale != nullptr) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] *= __ldg(p.scale + col0 + j);
+    for (int j = 0; j < 8; ++j) {
+      const float4 b = reinterpret_cast<const float4*>(bias32)[j];
+      v[4 * j] += b.x;
+      v[4 * j + 1] += b.y;
+      v[4 * j + 2] += b.z;
+      v[4 * j + 3] += b.w;
     }
-  } else if constexpr (MODE == EPI_RESID) {
+  }
+  if constexpr (MODE == EPI_F32 || MODE == EPI_RESID) {
+    if (scale32 != nullptr) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= __ldg(p.scale + col0 + j);
+      for (int j = 0; j < 8; ++j) {
+        const float4 c = reinterpret_cast<const float4*>(scale32)[j];
+        v[4 * j] *= c.x;
+        v[4 * j + 1] *= c.y;
+        v[4 * j + 2] *= c.z;
+        v[4 * j + 3] *= c.w;
+      }
+    }
   } else if constexpr (MODE == EPI_BF16_GELU || MODE == EPI_Q8_GELU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = FAST_GELU ? gelu_erf_fast(v[j]) : gelu_erf(v[j]);
@@ -128,7 +140,7 @@ __device__ __forceinline__ void epi_direct(const GemmEpi& p, int row, int col0, 
 
 template <int MODE>
 __device__ __forceinline__ void epilogue_chunk(const GemmEpi& p, int row, int col0, int N, float (&v)[32]) {
-  epi_math<MODE>(p, row, col0, v);
+  epi_math<MODE>(p, row, col0, v, p.bias ? p.bias + col0 : nullptr, p.scale ? p.scale + col0 : nullptr);
   epi_direct<MODE>(p, row, col0, N, v);
 }
 

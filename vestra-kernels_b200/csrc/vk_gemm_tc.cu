@@ -3,61 +3,65 @@
 // Replaces the reference's shape-specialised AVX-512 projections
 // (src/specialized.rs:770-1300: linear_f32_da3_base, linear_bias_scale_f32_da3_base,
 // qkv_f32_da3_base) and the separate bias / GELU / LayerScale / residual passes
-// (src/scalar.rs:65-155, src/dispatch.rs:56-77) with one persistent kernel:
+// (src/scalar.rs:65-155, src/dispatch.rs:56-77) with one persistent kernel,
+// C[M, N] = A[M, K] . W[N, K]^T (both K-major bf16, f32 accumulation):
 //
-//   warp 0      TMA producer: A [128 x 64] and W [BN x 64] bf16 tiles, 128B swizzle,
-//               into a STAGES-deep shared-memory ring (mbarrier full/empty pairs)
-//   warp 1      allocates TMEM, one elected lane issues tcgen05.mma (M=128, N=BN,
-//               K=16) into one of two f32 accumulators in TMEM (2 x BN columns)
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (one row per thread),
-//               fused bias / GELU / LayerScale+residual / head-major QKV+RoPE, store
+//   warp 0       TMA producer: A [128 x 64] and W [128 x 64] bf16 slabs, 128-byte
+//                swizzle, into a STAGES-deep shared-memory ring (full/empty mbarriers)
+//   warp 1       allocates TMEM; one elected lane issues tcgen05.mma into one of two
+//                f32 accumulators in TMEM (double buffer: the epilogue of tile i
+//                overlaps the MMAs of tile i+1)
+//   warps 2..9   epilogue, two warps per TMEM lane quadrant (each takes half of the
+//                tile's columns): tcgen05.ld 32 columns at a time, software-pipelined,
+//                bias / scale from shared memory, fused GELU / LayerScale / RoPE,
+//                swizzled staging + TMA store (TMA reduce-add for the residual)
 //
-// The accumulator double buffer lets the epilogue of tile i overlap the MMAs
-// of tile i+1.  Tiles are visited m-major across the persistent grid so the
-// CTAs resident at one time share A row-blocks in L2.
-#include <cudaTypedefs.h>
-
+// PAIR = false: one CTA per 128 x 128 tile (MMA M=128, N=128).
+// PAIR = true:  a cluster of two CTAs (one per SM) per 256 x 256 tile with
+//               tcgen05.mma.cta_group::2 (M=256 split over the two SMs' TMEM, each
+//               SM staging its 128 rows of A and half of the W tile); used when the
+//               problem fills every SM pair at least once.
+// Tiles are visited m-major over the persistent grid so the CTAs resident at one
+// time share A row-blocks in L2.
 #include <stdlib.h>
 #include <string.h>
 
-#include <mutex>
-
 #include "vk_common.cuh"
-#include "vk_internal.h"
 #include "vk_epilogue.cuh"
+#include "vk_internal.h"
 
 namespace vk {
 
 namespace {
-constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_THREADS = 320;
+constexpr int EPI_THREADS = 256;
+constexpr int SLAB_BYTES = 128 * BK * 2;  // one 128-row operand slab per stage
 
-template <int BN>
-struct GemmCfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;
-  // epilogue staging: 4 warps x 2 buffers x (32 rows x 128 B)
-  static constexpr int STAGE_OUT_BYTES = 4 * 2 * 4096;
-  static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + STAGE_OUT_BYTES + 256;
+template <int MODE, bool PAIR>
+struct Cfg {
+  static constexpr bool F32OUT = (MODE == EPI_F32 || MODE == EPI_RESID || MODE == EPI_QKV_F32);
+  static constexpr int TILE_M = PAIR ? 256 : 128;  // rows of C per tile
+  static constexpr int TILE_N = PAIR ? 256 : 128;  // columns of C per tile
+  static constexpr int TMEM_COLS = 2 * TILE_N;
+  static constexpr int WARP_COLS = TILE_N / 2;     // columns one epilogue warp handles
+  static constexpr int STAGE_BYTES = 2 * SLAB_BYTES;
+  static constexpr int OUT_BUF = F32OUT ? 4096 : 2048;  // 32 x 32 staging tile
+  static constexpr int OUT_BYTES = 8 * 2 * OUT_BUF;     // 8 warps, double buffered
+  static constexpr int BIAS_BYTES = 2 * TILE_N * 4;     // bias + scale of the tile
+  static constexpr int STAGES = F32OUT ? 4 : 5;
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + OUT_BYTES + BIAS_BYTES + 256;
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-// Output element size and the TMA swizzle of the 32 x 32 staging tile.
-template <int MODE>
-struct OutTraits {
-  static constexpr bool F32 = (MODE == EPI_F32 || MODE == EPI_RESID || MODE == EPI_QKV_F32);
-  static constexpr int ROW_BYTES = F32 ? 128 : 64;
-};
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(EPI_THREADS) : "memory"); }
 
 // Writes this thread's 32 values as row `lane` of a 32-row staging tile in
 // the TMA 128-byte (f32) or 64-byte (bf16) swizzle, so that the 16-byte
 // chunks of one store instruction spread over all banks.
-template <int MODE>
+template <bool F32>
 __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const float (&v)[32]) {
-  if constexpr (OutTraits<MODE>::F32) {
+  if constexpr (F32) {
     uint8_t* row = buf + lane * 128;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -74,15 +78,16 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const float (&
 }
 }  // namespace
 
-// Epilogue of one accumulator tile for one epilogue warp: rows
-// [row0, row0 + 32) of the output, columns [n0, n0 + BN_).  Reads TMEM 32
-// columns at a time, applies the fused epilogue and writes through a
-// swizzled staging buffer with TMA stores.  `release` runs once the
-// accumulator has been read completely (it hands it back to the MMA warp).
-template <int MODE, int BN_, class Release>
-__device__ __forceinline__ void epilogue_tile(const GemmEpi& epi, const CUtensorMap* tmO0, const CUtensorMap* tmO1,
-                                              const CUtensorMap* tmO2, int M, int N, int row0, int n0,
-                                              uint32_t tbase, uint8_t* stage, int& sb, int lane, Release release) {
+// Epilogue of one warp's share of an accumulator tile: rows [row0, row0+32),
+// columns [c0, c0 + NCOL).  `release` runs once the TMEM columns have all
+// been read (it hands the accumulator back to the MMA warp).
+template <int MODE, int NCOL, class Release>
+__device__ __forceinline__ void epilogue_part(const GemmEpi& epi, const CUtensorMap* tmO0, const CUtensorMap* tmO1,
+                                              const CUtensorMap* tmO2, int M, int N, int row0, int c0,
+                                              uint32_t tbase, const float* sbias, const float* sscale,
+                                              uint8_t* stage, int& sb, int lane, Release release) {
+  constexpr bool F32 = (MODE == EPI_F32 || MODE == EPI_RESID || MODE == EPI_QKV_F32);
+  constexpr int OUT_BUF = F32 ? 4096 : 2048;
   const int row = row0 + lane;
   // A 32-row chunk of the head-major QKV output that crosses an image
   // boundary (or the end of M) is written row by row instead of by TMA.
@@ -93,26 +98,29 @@ __device__ __forceinline__ void epilogue_tile(const GemmEpi& epi, const CUtensor
     t0 = row0 - img * epi.tokens;
     direct = (t0 + 32 > epi.tokens) || (row0 + 32 > M);
   }
-#pragma unroll 1
-  for (int c = 0; c < BN_ / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld32(tbase + static_cast<uint32_t>(c * 32), r);
+  uint32_t r[2][32];
+  tmem_ld32(tbase, r[0]);
+#pragma unroll
+  for (int c = 0; c < NCOL / 32; ++c) {
     tmem_wait_ld();
-    if (c == BN_ / 32 - 1) release();
+    if (c + 1 < NCOL / 32)
+      tmem_ld32(tbase + static_cast<uint32_t>((c + 1) * 32), r[(c + 1) & 1]);  // overlaps this chunk's math
+    else
+      release();
     if (row0 >= M) continue;
-    const int col0 = n0 + c * 32;
+    const int col0 = c0 + c * 32;
     float v[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-    epi_math<MODE, true>(epi, row, col0, v);
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[c & 1][j]);
+    epi_math<MODE, true>(epi, row, col0, v, sbias ? sbias + c * 32 : nullptr, sscale ? sscale + c * 32 : nullptr);
     if (direct) {
       if (row < M) epi_direct<MODE>(epi, row, col0, N, v);
       continue;
     }
-    uint8_t* buf = stage + sb * 4096;
+    uint8_t* buf = stage + sb * OUT_BUF;
     if (lane == 0) bulk_wait_read<1>();  // the store that last read `buf` is done with it
     __syncwarp();
-    stage_row<MODE>(buf, lane, v);
+    stage_row<F32>(buf, lane, v);
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) {
@@ -131,19 +139,20 @@ __device__ __forceinline__ void epilogue_tile(const GemmEpi& epi, const CUtensor
   }
 }
 
-// ------------------------------------------------------------------ kernel
-template <int BN, int MODE>
+template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmO0, const __grid_constant__ CUtensorMap tmO1,
                 const __grid_constant__ CUtensorMap tmO2, const GemmEpi epi, int M, int N, int K, int* err) {
-  using C = GemmCfg<BN>;
+  using C = Cfg<MODE, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint8_t* sB = smem + C::STAGES * SLAB_BYTES;
   uint8_t* sOut = smem + C::STAGES * C::STAGE_BYTES;  // 1024-aligned
-  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + C::STAGE_OUT_BYTES);
+  float* sBias = reinterpret_cast<float*>(sOut + C::OUT_BYTES);
+  float* sScale = sBias + C::TILE_N;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sScale + C::TILE_N);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -151,8 +160,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_tiles = (M + BM - 1) / BM;
-  const int n_tiles = N / BN;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit = PAIR ? (blockIdx.x >> 1) : blockIdx.x;  // CTA pair or CTA
+  const int units = PAIR ? (gridDim.x >> 1) : gridDim.x;
+  const int m_tiles = (M + C::TILE_M - 1) / C::TILE_M;
+  const int n_tiles = N / C::TILE_N;
   const int num_tiles = m_tiles * n_tiles;
   const int kb_n = K / BK;
 
@@ -163,20 +175,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], PAIR ? 16 : 8);  // one arrival per epilogue warp (of both CTAs)
     }
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_cg2(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish_cg2();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -185,171 +202,26 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * BM;
-        const int n0 = (tile % n_tiles) * BN;
+      for (int tile = unit; tile < num_tiles && ok; tile += units) {
+        const int m0 = (tile / n_tiles) * C::TILE_M + 128 * static_cast<int>(rank);
+        const int n0 = (tile % n_tiles) * C::TILE_N + 128 * static_cast<int>(rank);
         for (int kb = 0; kb < kb_n; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, err, VK_DEV_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, m0);
-          tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, n0);
+          if constexpr (PAIR) {
+            // both CTAs' slabs complete on the leader's barrier
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            const uint32_t bar = mapa_shared(&full[stage], 0);
+            tma_load_2d_cg2(sA + stage * SLAB_BYTES, &tmA, bar, kb * BK, m0);
+            tma_load_2d_cg2(sB + stage * SLAB_BYTES, &tmB, bar, kb * BK, n0);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            tma_load_2d(sA + stage * SLAB_BYTES, &tmA, &full[stage], kb * BK, m0);
+            tma_load_2d(sB + stage * SLAB_BYTES, &tmB, &full[stage], kb * BK, n0);
+          }
           if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(BM, BN);
-      int stage = 0;
-      uint32_t phase = 0;
-      int it = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
-        const int acc = it & 1;
-        const uint32_t aphase = (it >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], aphase ^ 1u, err, VK_DEV_TIMEOUT_MMA)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < kb_n; ++kb) {
-          if (!mbar_wait(&full[stage], phase, err, VK_DEV_TIMEOUT_MMA)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t adesc = smem_desc_k_sw128(smem_u32(sA + stage * C::A_BYTES));
-          const uint64_t bdesc = smem_desc_k_sw128(smem_u32(sB + stage * C::B_BYTES));
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_f16(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc + static_cast<uint64_t>(k * 2),
-                     idesc, (kb | k) != 0 ? 1u : 0u);
-          umma_commit(&empty[stage]);
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (ok) umma_commit(&tfull[acc]);
-      }
-    }
-  } else {
-    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32) are this warp's
-    uint8_t* stage = sOut + (warp - 2) * 2 * 4096;
-    int sb = 0;
-    int it = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
-      const int acc = it & 1;
-      const uint32_t aphase = (it >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], aphase, err, VK_DEV_TIMEOUT_EPILOGUE)) break;
-      tc_fence_after();
-      const int m0 = (tile / n_tiles) * BM;
-      const int n0 = (tile % n_tiles) * BN;
-      const int row0 = m0 + quad * 32;
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      epilogue_tile<MODE, BN>(epi, &tmO0, &tmO1, &tmO2, M, N, row0, n0, tbase, stage, sb, lane, [&] {
-        tc_fence_before();
-        mbar_arrive(&tempty[acc]);
-      });
-    }
-    if (lane == 0) bulk_wait<0>();
-  }
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
-  }
-}
-
-// ------------------------------------------------------------------ CTA-pair kernel
-// Same pipeline on a cluster of two CTAs (one per SM): the pair computes a
-// 256 x 256 tile with tcgen05.mma.cta_group::2 (M = 256 split across the two
-// SMs' TMEM, N = 256 with each SM staging half of the W tile).  Per SM this
-// halves the W bytes staged per FLOP, the bound of the single-CTA kernel.
-//   both CTAs   warp 0 loads its A rows [m0 + 128 r, +128) and W rows
-//               [n0 + 128 r, +128); both loads complete on the leader's
-//               barrier; warps 2..5 run the epilogue on their own TMEM rows
-//   leader      warp 1 issues the MMAs and commits to both CTAs' barriers
-namespace {
-constexpr int P_STAGES = 6;
-constexpr int P_A_BYTES = 128 * BK * 2;
-constexpr int P_B_BYTES = 128 * BK * 2;
-constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
-constexpr int P_STAGE_OUT_BYTES = 4 * 2 * 4096;
-constexpr size_t P_SMEM = 1024 + static_cast<size_t>(P_STAGES) * P_STAGE_BYTES + P_STAGE_OUT_BYTES + 256;
-}  // namespace
-
-template <int MODE>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
-    k_gemm_bf16_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmO0, const __grid_constant__ CUtensorMap tmO1,
-                     const __grid_constant__ CUtensorMap tmO2, const GemmEpi epi, int M, int N, int K, int* err) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + P_STAGES * P_A_BYTES;
-  uint8_t* sOut = smem + P_STAGES * P_STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + P_STAGE_OUT_BYTES);
-  uint64_t* empty = full + P_STAGES;
-  uint64_t* tfull = empty + P_STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();
-  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int m_tiles = (M + 255) / 256;
-  const int n_tiles = N / 256;
-  const int num_tiles = m_tiles * n_tiles;
-  const int kb_n = K / BK;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < P_STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);  // one arrival per epilogue warp of both CTAs
-    }
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc_cg2(tmem_slot, 512);
-    tmem_relinquish_cg2();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
-  }
-  tc_fence_before();
-  cluster_sync();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        const int m0 = (tile / n_tiles) * 256;
-        const int n0 = (tile % n_tiles) * 256;
-        for (int kb = 0; kb < kb_n; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, err, VK_DEV_TIMEOUT_PRODUCER)) {
-            ok = false;
-            break;
-          }
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
-          const uint32_t bar = mapa_shared(&full[stage], 0);
-          tma_load_2d_cg2(sA + stage * P_A_BYTES, &tmA, bar, kb * BK, m0 + 128 * static_cast<int>(rank));
-          tma_load_2d_cg2(sB + stage * P_B_BYTES, &tmB, bar, kb * BK, n0 + 128 * static_cast<int>(rank));
-          if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1u;
           }
@@ -358,229 +230,169 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = idesc_bf16(256, 256);
+      constexpr uint32_t idesc = idesc_bf16(C::TILE_M, C::TILE_N);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++it) {
+      for (int tile = unit; tile < num_tiles && ok; tile += units, ++it) {
         const int acc = it & 1;
         const uint32_t aphase = (it >> 1) & 1;
         if (!mbar_wait(&tempty[acc], aphase ^ 1u, err, VK_DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 256);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::TILE_N);
         for (int kb = 0; kb < kb_n; ++kb) {
           if (!mbar_wait(&full[stage], phase, err, VK_DEV_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = smem_desc_k_sw128(smem_u32(sA + stage * P_A_BYTES));
-          const uint64_t bdesc = smem_desc_k_sw128(smem_u32(sB + stage * P_B_BYTES));
+          const uint64_t adesc = smem_desc_k_sw128(smem_u32(sA + stage * SLAB_BYTES));
+          const uint64_t bdesc = smem_desc_k_sw128(smem_u32(sB + stage * SLAB_BYTES));
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_f16_cg2(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc + static_cast<uint64_t>(k * 2), idesc,
-                         (kb | k) != 0 ? 1u : 0u);
-          umma_commit_cg2_mc(&empty[stage], 0x3);
-          if (++stage == P_STAGES) {
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
+            if constexpr (PAIR)
+              umma_f16_cg2(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc + static_cast<uint64_t>(k * 2), idesc,
+                           accum);
+            else
+              umma_f16(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc + static_cast<uint64_t>(k * 2), idesc,
+                       accum);
+          }
+          if constexpr (PAIR) umma_commit_cg2_mc(&empty[stage], 0x3); else umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (ok) umma_commit_cg2_mc(&tfull[acc], 0x3);
+        if (ok) {
+          if constexpr (PAIR) umma_commit_cg2_mc(&tfull[acc], 0x3); else umma_commit(&tfull[acc]);
+        }
       }
     }
   } else {
-    const int quad = warp & 3;
-    uint8_t* stage = sOut + (warp - 2) * 2 * 4096;
+    const int ew = warp - 2;        // 0..7
+    const int quad = warp & 3;      // TMEM lanes [32*quad, 32*quad + 32) are this warp's
+    const int chalf = ew >> 2;      // which half of the tile's columns
+    const int et = threadIdx.x - 64;
+    uint8_t* stage = sOut + ew * 2 * C::OUT_BUF;
     int sb = 0;
     int it = 0;
-    for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
+    bool ok = true;
+    for (int tile = unit; tile < num_tiles && ok; tile += units, ++it) {
       const int acc = it & 1;
       const uint32_t aphase = (it >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], aphase, err, VK_DEV_TIMEOUT_EPILOGUE)) break;
+      const int m0 = (tile / n_tiles) * C::TILE_M;
+      const int n0 = (tile % n_tiles) * C::TILE_N;
+      // bias / scale of this tile's columns into shared memory (all 8 warps)
+      epi_sync();
+      for (int i = et; i < C::TILE_N; i += EPI_THREADS) {
+        if (epi.bias) sBias[i] = __ldg(epi.bias + n0 + i);
+        if (epi.scale) sScale[i] = __ldg(epi.scale + n0 + i);
+      }
+      epi_sync();
+      if (!mbar_wait(&tfull[acc], aphase, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+        ok = false;  // every epilogue warp gives up at the same tile
+        break;
+      }
       tc_fence_after();
-      const int m0 = (tile / n_tiles) * 256;
-      const int n0 = (tile % n_tiles) * 256;
       const int row0 = m0 + 128 * static_cast<int>(rank) + quad * 32;
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * 256);
-      epilogue_tile<MODE, 256>(epi, &tmO0, &tmO1, &tmO2, M, N, row0, n0, tbase, stage, sb, lane, [&] {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
-      });
+      const int c_off = chalf * C::WARP_COLS;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * C::TILE_N + c_off);
+      epilogue_part<MODE, C::WARP_COLS>(epi, &tmO0, &tmO1, &tmO2, M, N, row0, n0 + c_off, tbase,
+                                        epi.bias ? sBias + c_off : nullptr, epi.scale ? sScale + c_off : nullptr,
+                                        stage, sb, lane, [&] {
+                                          tc_fence_before();
+                                          __syncwarp();
+                                          if (lane == 0) {
+                                            if constexpr (PAIR)
+                                              mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
+                                            else
+                                              mbar_arrive(&tempty[acc]);
+                                          }
+                                        });
     }
     if (lane == 0) bulk_wait<0>();
   }
   tc_fence_before();
-  cluster_sync();
+  if constexpr (PAIR) cluster_sync(); else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_cg2(tmem_base, 512);
+    if constexpr (PAIR) tmem_dealloc_cg2(tmem_base, C::TMEM_COLS); else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
 // ------------------------------------------------------------------ host side
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
-                  uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
-                  CUtensorMapSwizzle swz) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return false;
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_stride_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
-                  uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
-                  CUtensorMapSwizzle swz) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return false;
-  cuuint64_t dims[3] = {d0, d1, d2};
-  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
-  cuuint32_t box[3] = {box0, box1, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
-
+namespace {
 struct OutMaps {
   CUtensorMap m[3];
 };
 
-template <int BN, int MODE>
-static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om, const GemmEpi& epi,
-                               int M, int N, int K, int* err, cudaStream_t s) {
-  using C = GemmCfg<BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_bf16<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(C::SMEM));
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
-  const int tiles = ((M + BM - 1) / BM) * (N / BN);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  k_gemm_bf16<BN, MODE><<<grid, GEMM_THREADS, C::SMEM, s>>>(ta, tb, om.m[0], om.m[1], om.m[2], epi, M, N, K, err);
-  return cudaGetLastError();
-}
-
-template <int MODE>
-static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om, const GemmEpi& epi,
-                               int M, int N, int K, int* err, cudaStream_t s) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_bf16_pair<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(P_SMEM));
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
-  const int tiles = ((M + 255) / 256) * (N / 256);
+template <int MODE, bool PAIR>
+cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om, const GemmEpi& epi, int M, int N,
+                   int K, int* err, cudaStream_t s) {
+  using C = Cfg<MODE, PAIR>;
+  static int max_units = 0;  // CTAs (or CTA pairs) that can be resident at once
   cudaLaunchConfig_t cfg = {};
-  static int max_pairs = 0;  // clusters of 2 that can be resident at once
-  if (max_pairs == 0) {
-    cudaLaunchConfig_t q = {};
-    q.gridDim = dim3(2 * (num_sms() / 2));
-    q.blockDim = dim3(GEMM_THREADS);
-    q.dynamicSmemBytes = P_SMEM;
-    cudaLaunchAttribute qa[1];
-    qa[0].id = cudaLaunchAttributeClusterDimension;
-    qa[0].val.clusterDim.x = 2;
-    qa[0].val.clusterDim.y = 1;
-    qa[0].val.clusterDim.z = 1;
-    q.attrs = qa;
-    q.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, k_gemm_bf16_pair<MODE>, &q) != cudaSuccess || n <= 0) n = num_sms() / 2;
-    max_pairs = n;
-  }
-  const int pairs = tiles < max_pairs ? tiles : max_pairs;
-  cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(GEMM_THREADS);
-  cfg.dynamicSmemBytes = P_SMEM;
+  cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_gemm_bf16_pair<MODE>, ta, tb, om.m[0], om.m[1], om.m[2], epi, M, N, K, err);
+  if (PAIR) {
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  if (max_units == 0) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_bf16<MODE, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(C::SMEM));
+    if (e != cudaSuccess) return e;
+    int n = 0;
+    if (PAIR) {
+      cfg.gridDim = dim3(2 * (num_sms() / 2));
+      if (cudaOccupancyMaxActiveClusters(&n, k_gemm_bf16<MODE, PAIR>, &cfg) != cudaSuccess || n <= 0) n = num_sms() / 2;
+    } else {
+      n = num_sms();
+    }
+    max_units = n;
+  }
+  const int tiles = ((M + C::TILE_M - 1) / C::TILE_M) * (N / C::TILE_N);
+  const int units = tiles < max_units ? tiles : max_units;
+  cfg.gridDim = dim3(PAIR ? 2 * units : units);
+  return cudaLaunchKernelEx(&cfg, k_gemm_bf16<MODE, PAIR>, ta, tb, om.m[0], om.m[1], om.m[2], epi, M, N, K, err);
 }
 
-static cudaError_t dispatch_pair(int mode, const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om,
-                                 const GemmEpi& epi, int M, int N, int K, int* err, cudaStream_t s) {
+template <bool PAIR>
+cudaError_t dispatch(int mode, const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om, const GemmEpi& epi,
+                     int M, int N, int K, int* err, cudaStream_t s) {
   switch (mode) {
-    case EPI_F32: return launch_pair<EPI_F32>(ta, tb, om, epi, M, N, K, err, s);
-    case EPI_BF16: return launch_pair<EPI_BF16>(ta, tb, om, epi, M, N, K, err, s);
-    case EPI_BF16_GELU: return launch_pair<EPI_BF16_GELU>(ta, tb, om, epi, M, N, K, err, s);
-    case EPI_RESID: return launch_pair<EPI_RESID>(ta, tb, om, epi, M, N, K, err, s);
-    case EPI_QKV_BF16: return launch_pair<EPI_QKV_BF16>(ta, tb, om, epi, M, N, K, err, s);
-    case EPI_QKV_F32: return launch_pair<EPI_QKV_F32>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_F32: return launch<EPI_F32, PAIR>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_BF16: return launch<EPI_BF16, PAIR>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_BF16_GELU: return launch<EPI_BF16_GELU, PAIR>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_RESID: return launch<EPI_RESID, PAIR>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_QKV_BF16: return launch<EPI_QKV_BF16, PAIR>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_QKV_F32: return launch<EPI_QKV_F32, PAIR>(ta, tb, om, epi, M, N, K, err, s);
     default: return cudaErrorInvalidValue;
   }
 }
-
-template <int BN>
-static cudaError_t dispatch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om,
-                                 const GemmEpi& epi, int M, int N, int K, int* err, cudaStream_t s) {
-  switch (mode) {
-    case EPI_F32: return launch_gemm<BN, EPI_F32>(ta, tb, om, epi, M, N, K, err, s);
-    case EPI_BF16: return launch_gemm<BN, EPI_BF16>(ta, tb, om, epi, M, N, K, err, s);
-    case EPI_BF16_GELU: return launch_gemm<BN, EPI_BF16_GELU>(ta, tb, om, epi, M, N, K, err, s);
-    case EPI_RESID: return launch_gemm<BN, EPI_RESID>(ta, tb, om, epi, M, N, K, err, s);
-    case EPI_QKV_BF16: return launch_gemm<BN, EPI_QKV_BF16>(ta, tb, om, epi, M, N, K, err, s);
-    case EPI_QKV_F32: return launch_gemm<BN, EPI_QKV_F32>(ta, tb, om, epi, M, N, K, err, s);
-    default: return cudaErrorInvalidValue;
-  }
-}
+}  // namespace
 
 cudaError_t gemm_bf16_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, int M, int N, int K, int mode,
                          const GemmEpi& epi, int* err, cudaStream_t s) {
   if (M <= 0 || N <= 0 || K <= 0 || K % BK != 0 || N % 128 != 0) return cudaErrorInvalidValue;
   if (mode == EPI_RESID && epi.scale == nullptr) return cudaErrorInvalidValue;
-  // Wide tiles when they still give at least one full wave of CTAs.
-  const int m_tiles = (M + BM - 1) / BM;
-  const bool wide = (N % 256 == 0) && m_tiles * (N / 256) >= num_sms();
-  // CTA pairs (256 x 256 tiles) when they fill every SM at least once.
+  // CTA pairs (256 x 256 tiles) when they fill every SM pair at least once.
   static const bool pair_enabled = getenv("VK_GEMM_NO_PAIR") == nullptr;
   const bool pair = pair_enabled && (N % 256 == 0) && ((M + 255) / 256) * (N / 256) >= num_sms() / 2;
-  const int bn = pair ? 128 : (wide ? 256 : 128);
   CUtensorMap ta, tb;
-  if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, A, K, M, static_cast<uint64_t>(K) * 2, BK, BM,
+  if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, A, K, M, static_cast<uint64_t>(K) * 2, BK, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, W, K, N, static_cast<uint64_t>(K) * 2, BK, bn,
+  if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, W, K, N, static_cast<uint64_t>(K) * 2, BK, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   OutMaps om;
@@ -603,9 +415,8 @@ cudaError_t gemm_bf16_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, int M, 
     ok = make_tmap_2d(&om.m[0], odt, epi.out, N, M, static_cast<uint64_t>(epi.ldo) * esz, 32, 32, oswz);
   }
   if (!ok) return cudaErrorInvalidValue;
-  if (pair) return dispatch_pair(mode, ta, tb, om, epi, M, N, K, err, s);
-  return wide ? dispatch_mode<256>(mode, ta, tb, om, epi, M, N, K, err, s)
-              : dispatch_mode<128>(mode, ta, tb, om, epi, M, N, K, err, s);
+  return pair ? dispatch<true>(mode, ta, tb, om, epi, M, N, K, err, s)
+              : dispatch<false>(mode, ta, tb, om, epi, M, N, K, err, s);
 }
 
 }  // namespace vk
