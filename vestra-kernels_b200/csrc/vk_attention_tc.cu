@@ -12,10 +12,12 @@
 //   warp 1      TMEM owner; one lane issues
 //                 S(j) = Q K_j^T        (M=128, N=128, K=64; A, B from smem)
 //                 O(j) = P(j) V_j        (M=128, N=64, K=128; A = P from TMEM)
-//   warps 2..5  one query row per thread: read S(j) from TMEM, running max,
-//               p = 2^(s*log2e/8 - m), row sum, P(j) -> TMEM as bf16; fold
-//               O(j-1) into f32 registers with the max correction; finally
-//               normalise and store token-major bf16 / Q8_0 or head-major f32.
+//   warps 2..5  one query row per thread: S(j) from TMEM into registers (S is
+//               released at once so S(j+1) overlaps this block's exponentials),
+//               block max, p = 2^(s*log2e/8 - m_ref), row sum, P(j) -> TMEM as
+//               bf16.  O accumulates in TMEM over all blocks; it is rescaled
+//               only when the running max passes m_ref by more than 2^8.
+//               Finally O / l is stored token-major bf16 / Q8_0 or head-major f32.
 // TMEM: S at columns [0,128), P at [128,192) (bf16 pairs), O at [192,256).
 #include "vk_common.cuh"
 #include "vk_internal.h"
@@ -50,8 +52,7 @@ __global__ void __launch_bounds__(A_THREADS, 2)
   uint64_t* s_empty = s_full + 1;
   uint64_t* p_full = s_empty + 1;
   uint64_t* o_full = p_full + 1;
-  uint64_t* o_empty = o_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
@@ -68,7 +69,6 @@ __global__ void __launch_bounds__(A_THREADS, 2)
     mbar_init(s_empty, 128);
     mbar_init(p_full, 128);
     mbar_init(o_full, 1);
-    mbar_init(o_empty, 128);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -115,14 +115,13 @@ __global__ void __launch_bounds__(A_THREADS, 2)
       for (int j = 0; j < nb && ok; ++j) {
         if (j + 1 < nb && !issue_s(j + 1)) break;
         if (!mbar_wait(p_full, j & 1, err, VK_DEV_TIMEOUT_MMA)) break;
-        if (!mbar_wait(o_empty, (j & 1) ^ 1, err, VK_DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
         const int st = j % AST;
         const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(sV + st * TILE_BYTES));
 #pragma unroll
         for (int k = 0; k < AKV / 16; ++k)
           umma_f16_ts(tmem + COL_O, tmem + COL_P + static_cast<uint32_t>(k * 8),
-                      vdesc + static_cast<uint64_t>(k * (2048 >> 4)), idO, k > 0 ? 1u : 0u);
+                      vdesc + static_cast<uint64_t>(k * (2048 >> 4)), idO, (j | k) > 0 ? 1u : 0u);
         umma_commit(o_full);
         umma_commit(&kv_empty[st]);
       }
@@ -132,68 +131,78 @@ __global__ void __launch_bounds__(A_THREADS, 2)
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const int qrow = q0 + quad * 32 + lane;
     const float sl2 = 0.125f * 1.4426950408889634f;  // (1/sqrt(64)) * log2(e)
-    float o[64];
-#pragma unroll
-    for (int d = 0; d < 64; ++d) o[d] = 0.0f;
-    float m_run = -INFINITY;  // running max of s * sl2
-    float m_o = -INFINITY;    // normalisation of o[]
+    // O accumulates in TMEM across blocks, normalised to m_ref; m_ref only
+    // moves (and O, l are rescaled) when the running max exceeds it by more
+    // than 2^8, so p = 2^(s*sl2 - m_ref) stays below 256.
+    float m_ref = -INFINITY;
     float l_run = 0.0f;
     bool ok = true;
-    float m_prev = -INFINITY;  // max after the previous block (normalisation of O(j-1))
     for (int j = 0; j < nb && ok; ++j) {
       if (!mbar_wait(s_full, j & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int kbase = j * AKV;
-      const int valid = tokens - kbase;  // keys of this block that exist (may exceed 128)
-      // pass 1: block max
-      float bmax = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + COL_S + c * 32, r);
-        tmem_wait_ld();
+      uint32_t r[128];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c * 32 + i < valid) bmax = fmaxf(bmax, __uint_as_float(r[i]));
+      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + COL_S + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(s_empty);  // S is in registers: the MMA may compute S(j+1) now
+      const int valid = tokens - j * AKV;
+      const bool full_block = valid >= AKV;
+      float bmax = -INFINITY;
+      if (full_block) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) bmax = fmaxf(bmax, __uint_as_float(r[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i < valid) bmax = fmaxf(bmax, __uint_as_float(r[i]));
       }
-      const float m_new = fmaxf(m_run, bmax * sl2);
-      // fold the previous block's output while the tensor core computes
+      const float m_blk = bmax * sl2;
+      bool rescale = false;
+      float f = 1.0f;
+      if (j == 0) {
+        m_ref = m_blk;
+      } else if (m_blk > m_ref + 8.0f) {
+        rescale = true;
+        f = ex2_approx(m_ref - m_blk);
+        m_ref = m_blk;
+      }
       if (j > 0) {
-        uint32_t r0[32], r1[32];
+        // O(j-1) done: P may be overwritten and O rescaled
         if (!mbar_wait(o_full, (j - 1) & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const float f = (m_o == -INFINITY) ? 0.0f : ex2_approx(m_o - m_prev);
-        tmem_ld32(tmem + lane_base + COL_O, r0);
-        tmem_wait_ld();
+        if (__any_sync(0xffffffffu, rescale)) {  // TMEM access is warp-collective
 #pragma unroll
-        for (int d = 0; d < 32; ++d) o[d] = o[d] * f + __uint_as_float(r0[d]);
-        tmem_ld32(tmem + lane_base + COL_O + 32, r1);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(o_empty);
+          for (int h = 0; h < 2; ++h) {
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_base + COL_O + h * 32, o);
+            tmem_wait_ld();
 #pragma unroll
-        for (int d = 0; d < 32; ++d) o[32 + d] = o[32 + d] * f + __uint_as_float(r1[d]);
-        m_o = m_prev;
+            for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * f);
+            tmem_st32(tmem + lane_base + COL_O + h * 32, o);
+          }
+          l_run *= f;
+        }
       }
-      // pass 2: probabilities -> P (bf16 pairs) in TMEM, row sum
       float bsum = 0.0f;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + COL_S + c * 32, r);
-        tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int k0 = c * 32 + 2 * i;
-          const float p0 = k0 < valid ? ex2_approx(fmaf(__uint_as_float(r[2 * i]), sl2, -m_new)) : 0.0f;
-          const float p1 = k0 + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), sl2, -m_new)) : 0.0f;
+          float p0 = ex2_approx(fmaf(__uint_as_float(r[k0]), sl2, -m_ref));
+          float p1 = ex2_approx(fmaf(__uint_as_float(r[k0 + 1]), sl2, -m_ref));
+          if (!full_block) {
+            p0 = k0 < valid ? p0 : 0.0f;
+            p1 = k0 + 1 < valid ? p1 : 0.0f;
+          }
           bsum += p0 + p1;
           pk[i] = pack_bf16x2(p0, p1);
         }
@@ -201,26 +210,21 @@ __global__ void __launch_bounds__(A_THREADS, 2)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(s_empty);
       mbar_arrive(p_full);
-      l_run = l_run * ((m_run == -INFINITY) ? 0.0f : ex2_approx(m_run - m_new)) + bsum;
-      m_prev = m_new;
-      m_run = m_new;
+      l_run += bsum;
     }
     if (ok && mbar_wait(o_full, (nb - 1) & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
-      // o is normalised to m_o, the last block's O to m_run
       tc_fence_after();
-      uint32_t r0[32];
-      const float f = (m_o == -INFINITY) ? 0.0f : ex2_approx(m_o - m_run);
+      float o[64];
       const float inv = 1.0f / l_run;
-      tmem_ld32(tmem + lane_base + COL_O, r0);
-      tmem_wait_ld();
 #pragma unroll
-      for (int d = 0; d < 32; ++d) o[d] = (o[d] * f + __uint_as_float(r0[d])) * inv;
-      tmem_ld32(tmem + lane_base + COL_O + 32, r0);
-      tmem_wait_ld();
+      for (int h = 0; h < 2; ++h) {
+        uint32_t r0[32];
+        tmem_ld32(tmem + lane_base + COL_O + h * 32, r0);
+        tmem_wait_ld();
 #pragma unroll
-      for (int d = 0; d < 32; ++d) o[32 + d] = (o[32 + d] * f + __uint_as_float(r0[d])) * inv;
+        for (int d = 0; d < 32; ++d) o[h * 32 + d] = __uint_as_float(r0[d]) * inv;
+      }
       if (qrow < tokens) {
         const int b_img = bh / heads, h = bh - b_img * heads;
         if constexpr (OUT == ATTN_OUT_HEAD_F32) {
