@@ -374,13 +374,21 @@ __device__ __forceinline__ float gelu_erf(float v) {
 
 // The same GELU with the fast exponential and division, for results that are
 // rounded to bf16 right after (error far below half a bf16 ulp).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float gelu_erf_fast(float v) {
-  const float x = fabsf(v) * 0.70710678118654752440f;
-  const float t = __fdividef(1.0f, 1.0f + 0.3275911f * x);
-  const float poly =
-      ((((1.0614054f * t - 1.453152f) * t) + 1.4214137f) * t - 0.28449674f) * t + 0.2548296f;
-  const float e = 1.0f - poly * t * __expf(-x * x);
-  return 0.5f * v * (1.0f + ((__float_as_uint(v) >> 31) ? -e : e));
+  // Same A&S 7.1.26 formula with the constants folded:
+  //   u = |v| * sqrt(log2 e) / sqrt(2),  t = 1 / (1 + (0.3275911 / sqrt(log2 e)) u),
+  //   exp(-v^2 / 2) = 2^(-u^2),  gelu = v/2 + |v|/2 * (1 - poly(t) * t * 2^(-u^2))
+  const float u = fabsf(v) * 0.84932180028801904272f;        // sqrt(log2 e) / sqrt(2)
+  const float t = rcp_approx(fmaf(0.27273748f, u, 1.0f));    // 0.3275911 / sqrt(log2 e)
+  const float pt = t * fmaf(fmaf(fmaf(fmaf(1.0614054f, t, -1.453152f), t, 1.4214137f), t, -0.28449674f), t, 0.2548296f);
+  const float y = fmaf(-pt, ex2_approx(-u * u), 1.0f);       // erf(|v| / sqrt 2)
+  const float h = 0.5f * v;
+  return fmaf(fabsf(h), y, h);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -19,6 +19,8 @@
 // graph on its second call and replayed afterwards.
 #include <stdlib.h>
 
+#include <algorithm>
+
 #include <vector>
 
 #include "vestra_b200.h"
@@ -109,12 +111,24 @@ int ensure_rope(vk_encoder* enc, size_t gh, size_t gw) {
     enc->graphs.clear();
     enc->seen.clear();
   }
-  VK_TRY_CUDA(cudaMalloc(&enc->rope, rot.size() * sizeof(float)), "rotation table");
-  VK_TRY_CUDA(cudaMemcpy(enc->rope, rot.data(), rot.size() * sizeof(float), cudaMemcpyHostToDevice), "rotation table");
+  // Two layouts of the same values: [t][axis][i](sin, cos) for the f32 RoPE
+  // pass, and [axis * 16 + i][t](sin, cos) for the GEMM epilogue, where the
+  // 32 threads of a warp hold 32 consecutive tokens (coalesced reads).
+  std::vector<float> both(2 * rot.size());
+  std::copy(rot.begin(), rot.end(), both.begin());
+  for (size_t t = 0; t < T; ++t)
+    for (size_t ai = 0; ai < 32; ++ai) {
+      both[rot.size() + (ai * T + t) * 2] = rot[(t * 32 + ai) * 2];
+      both[rot.size() + (ai * T + t) * 2 + 1] = rot[(t * 32 + ai) * 2 + 1];
+    }
+  VK_TRY_CUDA(cudaMalloc(&enc->rope, both.size() * sizeof(float)), "rotation table");
+  VK_TRY_CUDA(cudaMemcpy(enc->rope, both.data(), both.size() * sizeof(float), cudaMemcpyHostToDevice), "rotation table");
   enc->rope_h = gh;
   enc->rope_w = gw;
   return VK_OK;
 }
+
+size_t rope_tokens(const vk_encoder* enc) { return enc->rope_h * enc->rope_w + 1; }
 
 // Enqueues one forward on `s`; returns the number of kernels launched or a
 // negative value on a launch error.
@@ -150,7 +164,7 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
     fc2.resid = x;
     fc2.ldo = E;
     if (math == VK_MATH_BF16) {
-      qkv.q = a.q16; qkv.k = a.k16; qkv.v = a.v16; qkv.rope = enc->rope;
+      qkv.q = a.q16; qkv.k = a.k16; qkv.v = a.v16; qkv.rope = enc->rope + (rope_tokens(enc) * 64);
       fc1.out = a.h16;
       VK_L(layernorm_f32(x, nullptr, a.ln16, nullptr, nullptr, M, E, L.ln1_g, L.ln1_b, eps, s));
       VK_L(gemm_bf16_tc(a.ln16, L.qkv_w16, M, 3 * E, E, EPI_QKV_BF16, qkv, d_err, s));
@@ -160,7 +174,7 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
       VK_L(gemm_bf16_tc(a.ln16, L.fc1_w16, M, F, E, EPI_BF16_GELU, fc1, d_err, s));
       VK_L(gemm_bf16_tc(a.h16, L.fc2_w16, M, E, F, EPI_RESID, fc2, d_err, s));
     } else if (math == VK_MATH_Q8_0) {
-      qkv.q = a.q16; qkv.k = a.k16; qkv.v = a.v16; qkv.rope = enc->rope;
+      qkv.q = a.q16; qkv.k = a.k16; qkv.v = a.v16; qkv.rope = enc->rope + (rope_tokens(enc) * 64);
       fc1.q8 = a.hq;
       fc1.q8d = a.hd;
       VK_L(layernorm_f32(x, nullptr, nullptr, a.lnq, a.lnd, M, E, L.ln1_g, L.ln1_b, eps, s));

@@ -61,10 +61,10 @@ __device__ __forceinline__ void epi_math(const GemmEpi& p, int row, int col0, fl
     if (p.rope != nullptr && q.g < 2) {
       // Axial RoPE, rotate-half pairing (i, i + 16) inside this 32-wide axis
       // half (src/rope.rs:84-93); the chunk is exactly one axis half.
-      const float2* r = reinterpret_cast<const float2*>(p.rope + static_cast<size_t>(q.t) * 64 + q.axis * 32);
+      const float2* r = reinterpret_cast<const float2*>(p.rope) + static_cast<size_t>(q.axis * 16) * p.tokens + q.t;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float2 sc = __ldg(r + i);  // (sin, cos)
+        const float2 sc = __ldg(r + static_cast<size_t>(i) * p.tokens);  // (sin, cos)
         const float a = v[i], b = v[i + 16];
         v[i] = a * sc.y - b * sc.x;
         v[i + 16] = b * sc.y + a * sc.x;
