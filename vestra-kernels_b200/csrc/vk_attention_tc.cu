@@ -5,58 +5,64 @@
 // path (src/specialized.rs:730-765, 1400-1562; src/attention.rs:111-201):
 // non-causal softmax(Q K^T / 8) V with an online softmax over key blocks.
 //
-// One CTA = one (image, head) and 128 queries; 2 CTAs per SM share the SM
-// (256 TMEM columns each) so one CTA's softmax overlaps the other's MMAs.
+// One CTA per SM handles two 128-query tiles (A and B) of one (image, head)
+// so every K/V block is loaded once for 256 queries and the two tiles
+// ping-pong on the tensor core: while the softmax warps of A work on S_A(j),
+// the tensor core computes S_B(j), O_A(j-1) and S_A(j+1).
 //
-//   warp 0      TMA: Q tile once, then K and V blocks of 128 keys (2 stages)
-//   warp 1      TMEM owner; one lane issues
-//                 S(j) = Q K_j^T        (M=128, N=128, K=64; A, B from smem)
-//                 O(j) = P(j) V_j        (M=128, N=64, K=128; A = P from TMEM)
-//   warps 2..5  one query row per thread: S(j) from TMEM into registers (S is
-//               released at once so S(j+1) overlaps this block's exponentials),
-//               block max, p = 2^(s*log2e/8 - m_ref), row sum, P(j) -> TMEM as
-//               bf16.  O accumulates in TMEM over all blocks; it is rescaled
-//               only when the running max passes m_ref by more than 2^8.
-//               Finally O / l is stored token-major bf16 / Q8_0 or head-major f32.
-// TMEM: S at columns [0,128), P at [128,192) (bf16 pairs), O at [192,256).
+//   warp 0      TMA: the two Q tiles once, then K and V blocks of 128 keys
+//               (AST-stage ring shared by both tiles)
+//   warp 1      TMEM owner; one lane issues, per tile t and key block j,
+//                 S_t(j) = Q_t K_j^T     (M=128, N=128, K=64; A, B from smem)
+//                 O_t   += P_t(j) V_j     (M=128, N=64, K=128; A = P_t from TMEM)
+//   warps 2..5  softmax of tile A, warps 6..9 of tile B, one query row per
+//               thread: two passes over S in TMEM (block max, then
+//               p = 2^(s*log2e/8 - m_ref), row sum, P -> TMEM as bf16), 32
+//               columns at a time so nothing spills; the other tile keeps the
+//               tensor core busy while this one holds its S.  O
+//               accumulates in TMEM; it is rescaled only when the block max
+//               passes m_ref by more than 2^8.  Finally O / l is stored
+//               token-major bf16 / Q8_0 or head-major f32.
+// TMEM per tile: S [0,128), P [128,192) (bf16 pairs), O [192,256); tile B at +256.
 #include "vk_common.cuh"
 #include "vk_internal.h"
 
 namespace vk {
 
 namespace {
-constexpr int AQ = 128;       // queries per CTA
-constexpr int AKV = 128;      // keys per block
-constexpr int AST = 2;        // K/V pipeline stages
-constexpr int A_THREADS = 192;
+constexpr int AQ = 128;        // queries per tile
+constexpr int AKV = 128;       // keys per block
+constexpr int AST = 4;         // K/V pipeline stages
+constexpr int A_THREADS = 320; // producer, MMA, 2 x 4 softmax warps
 constexpr int TILE_BYTES = 128 * 128;  // 128 rows x 64 bf16
-constexpr uint32_t COL_S = 0, COL_P = 128, COL_O = 192;
-constexpr size_t ATT_SMEM = 1024 + TILE_BYTES * (1 + 2 * AST) + 256;
+constexpr uint32_t COL_S = 0, COL_P = 128, COL_O = 192, TILE_COLS = 256;
+constexpr size_t ATT_SMEM = 1024 + TILE_BYTES * (2 + 2 * AST) + 256;
 }  // namespace
 
 template <int OUT>
-__global__ void __launch_bounds__(A_THREADS, 2)
+__global__ void __launch_bounds__(A_THREADS, 1)
     k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, int heads, int tokens, void* out, __half* out_q8d,
                    int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + TILE_BYTES;
+  uint8_t* sQ = smem;  // tile A, then tile B
+  uint8_t* sK = smem + 2 * TILE_BYTES;
   uint8_t* sV = sK + AST * TILE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + AST * TILE_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_full = q_full + 1;
   uint64_t* kv_empty = kv_full + AST;
-  uint64_t* s_full = kv_empty + AST;
-  uint64_t* s_empty = s_full + 1;
-  uint64_t* p_full = s_empty + 1;
-  uint64_t* o_full = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
+  uint64_t* s_full = kv_empty + AST;  // [2]
+  uint64_t* s_empty = s_full + 2;     // [2]
+  uint64_t* p_full = s_empty + 2;     // [2]
+  uint64_t* o_full = p_full + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
-  const int q0 = blockIdx.x * AQ;
+  const int q0 = blockIdx.x * 2 * AQ;
+  const int ntiles = (tokens - q0 > AQ) ? 2 : 1;  // tile B may not exist
   const int nb = (tokens + AKV - 1) / AKV;
 
   if (threadIdx.x == 0) {
@@ -65,14 +71,16 @@ __global__ void __launch_bounds__(A_THREADS, 2)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_empty, 128);
-    mbar_init(p_full, 128);
-    mbar_init(o_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_empty[t], 128);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&o_full[t], 1);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -82,8 +90,8 @@ __global__ void __launch_bounds__(A_THREADS, 2)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_3d(sQ, &tmQ, q_full, 0, q0, bh);
+      mbar_arrive_expect_tx(q_full, ntiles * TILE_BYTES);
+      for (int t = 0; t < ntiles; ++t) tma_load_3d(sQ + t * TILE_BYTES, &tmQ, q_full, 0, q0 + t * AQ, bh);
       for (int j = 0; j < nb; ++j) {
         const int st = j % AST;
         if (!mbar_wait(&kv_empty[st], ((j / AST) & 1) ^ 1, err, VK_DEV_TIMEOUT_PRODUCER)) break;
@@ -97,70 +105,80 @@ __global__ void __launch_bounds__(A_THREADS, 2)
       constexpr uint32_t idS = idesc_bf16(128, 128);
       constexpr uint32_t idO = idesc_bf16_bmn(128, 64);
       bool ok = mbar_wait(q_full, 0, err, VK_DEV_TIMEOUT_MMA);
-      const uint64_t qdesc = smem_desc_k_sw128(smem_u32(sQ));
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % AST;
-        if (!mbar_wait(&kv_full[st], (j / AST) & 1, err, VK_DEV_TIMEOUT_MMA)) return false;
-        if (j > 0 && !mbar_wait(s_empty, (j - 1) & 1, err, VK_DEV_TIMEOUT_MMA)) return false;
+      auto issue_s = [&](int t, int j) -> bool {  // K_j must be resident
+        if (j > 0 && !mbar_wait(&s_empty[t], (j - 1) & 1, err, VK_DEV_TIMEOUT_MMA)) return false;
         tc_fence_after();
-        const uint64_t kdesc = smem_desc_k_sw128(smem_u32(sK + st * TILE_BYTES));
+        const uint64_t qdesc = smem_desc_k_sw128(smem_u32(sQ + t * TILE_BYTES));
+        const uint64_t kdesc = smem_desc_k_sw128(smem_u32(sK + (j % AST) * TILE_BYTES));
+        const uint32_t d = tmem + t * TILE_COLS + COL_S;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_f16(tmem + COL_S, qdesc + static_cast<uint64_t>(k * 2), kdesc + static_cast<uint64_t>(k * 2), idS,
-                   k > 0 ? 1u : 0u);
-        umma_commit(s_full);
+          umma_f16(d, qdesc + static_cast<uint64_t>(k * 2), kdesc + static_cast<uint64_t>(k * 2), idS, k > 0 ? 1u : 0u);
+        umma_commit(&s_full[t]);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < nb && ok; ++j) {
-        if (j + 1 < nb && !issue_s(j + 1)) break;
-        if (!mbar_wait(p_full, j & 1, err, VK_DEV_TIMEOUT_MMA)) break;
+      auto issue_o = [&](int t, int j) -> bool {
+        if (!mbar_wait(&p_full[t], j & 1, err, VK_DEV_TIMEOUT_MMA)) return false;
         tc_fence_after();
-        const int st = j % AST;
-        const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(sV + st * TILE_BYTES));
+        const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(sV + (j % AST) * TILE_BYTES));
+        const uint32_t base = tmem + t * TILE_COLS;
 #pragma unroll
         for (int k = 0; k < AKV / 16; ++k)
-          umma_f16_ts(tmem + COL_O, tmem + COL_P + static_cast<uint32_t>(k * 8),
+          umma_f16_ts(base + COL_O, base + COL_P + static_cast<uint32_t>(k * 8),
                       vdesc + static_cast<uint64_t>(k * (2048 >> 4)), idO, (j | k) > 0 ? 1u : 0u);
-        umma_commit(o_full);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&o_full[t]);
+        return true;
+      };
+      if (ok) ok = mbar_wait(&kv_full[0], 0, err, VK_DEV_TIMEOUT_MMA);
+      for (int t = 0; t < ntiles && ok; ++t) ok = issue_s(t, 0);
+      for (int j = 0; j < nb && ok; ++j) {
+        // per tile, as soon as its softmax has finished with S(j): S(j+1)
+        // (the next critical step of that tile), then O += P(j) V(j)
+        if (j + 1 < nb) ok = mbar_wait(&kv_full[(j + 1) % AST], ((j + 1) / AST) & 1, err, VK_DEV_TIMEOUT_MMA);
+        for (int t = 0; t < ntiles && ok; ++t) {
+          ok = mbar_wait(&p_full[t], j & 1, err, VK_DEV_TIMEOUT_MMA);
+          if (ok && j + 1 < nb) ok = issue_s(t, j + 1);
+          if (ok) ok = issue_o(t, j);
+        }
+        if (ok) umma_commit(&kv_empty[j % AST]);  // after every MMA that read stage j
       }
     }
   } else {
+    const int t = (warp - 2) >> 2;  // tile of this softmax warp
     const int quad = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-    const int qrow = q0 + quad * 32 + lane;
+    const uint32_t tb = tmem + t * TILE_COLS;
+    const int qrow = q0 + t * AQ + quad * 32 + lane;
     const float sl2 = 0.125f * 1.4426950408889634f;  // (1/sqrt(64)) * log2(e)
-    // O accumulates in TMEM across blocks, normalised to m_ref; m_ref only
-    // moves (and O, l are rescaled) when the running max exceeds it by more
-    // than 2^8, so p = 2^(s*sl2 - m_ref) stays below 256.
     float m_ref = -INFINITY;
     float l_run = 0.0f;
-    bool ok = true;
+    bool ok = t < ntiles;
     for (int j = 0; j < nb && ok; ++j) {
-      if (!mbar_wait(s_full, j & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+      if (!mbar_wait(&s_full[t], j & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t r[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + COL_S + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(s_empty);  // S is in registers: the MMA may compute S(j+1) now
       const int valid = tokens - j * AKV;
       const bool full_block = valid >= AKV;
-      float bmax = -INFINITY;
-      if (full_block) {
+      // pass 1: block max, 32 TMEM columns at a time
+      float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int i = 0; i < 128; ++i) bmax = fmaxf(bmax, __uint_as_float(r[i]));
-      } else {
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tb + lane_base + COL_S + c * 32, r);
+        tmem_wait_ld();
+        if (full_block) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i < valid) bmax = fmaxf(bmax, __uint_as_float(r[i]));
+          for (int i = 0; i < 32; i += 2)
+            pm[(i >> 1) & 3] = max3f(pm[(i >> 1) & 3], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i < valid) pm[i & 3] = fmaxf(pm[i & 3], __uint_as_float(r[i]));
+        }
       }
-      const float m_blk = bmax * sl2;
+      const float m_blk = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])) * sl2;
       bool rescale = false;
       float f = 1.0f;
       if (j == 0) {
@@ -172,7 +190,7 @@ __global__ void __launch_bounds__(A_THREADS, 2)
       }
       if (j > 0) {
         // O(j-1) done: P may be overwritten and O rescaled
-        if (!mbar_wait(o_full, (j - 1) & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+        if (!mbar_wait(&o_full[t], (j - 1) & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
           ok = false;
           break;
         }
@@ -181,46 +199,52 @@ __global__ void __launch_bounds__(A_THREADS, 2)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             uint32_t o[32];
-            tmem_ld32(tmem + lane_base + COL_O + h * 32, o);
+            tmem_ld32(tb + lane_base + COL_O + h * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * f);
-            tmem_st32(tmem + lane_base + COL_O + h * 32, o);
+            tmem_st32(tb + lane_base + COL_O + h * 32, o);
           }
           l_run *= f;
         }
       }
-      float bsum = 0.0f;
+      // pass 2: probabilities -> P (bf16 pairs), row sum
+      float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+      const float2 scale2 = make_float2(sl2, sl2), shift2 = make_float2(-m_ref, -m_ref);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tb + lane_base + COL_S + c * 32, r);
+        tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int k0 = c * 32 + 2 * i;
-          float p0 = ex2_approx(fmaf(__uint_as_float(r[k0]), sl2, -m_ref));
-          float p1 = ex2_approx(fmaf(__uint_as_float(r[k0 + 1]), sl2, -m_ref));
+          const float2 x = ffma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), scale2, shift2);
+          float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
           if (!full_block) {
-            p0 = k0 < valid ? p0 : 0.0f;
-            p1 = k0 + 1 < valid ? p1 : 0.0f;
+            p.x = k0 < valid ? p.x : 0.0f;
+            p.y = k0 + 1 < valid ? p.y : 0.0f;
           }
-          bsum += p0 + p1;
-          pk[i] = pack_bf16x2(p0, p1);
+          ps[i & 1] = fadd2(ps[i & 1], p);
+          pk[i] = pack_bf16x2(p.x, p.y);
         }
-        tmem_st16(tmem + lane_base + COL_P + c * 16, pk);
+        tmem_st16(tb + lane_base + COL_P + c * 16, pk);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
-      l_run += bsum;
+      mbar_arrive(&s_empty[t]);
+      mbar_arrive(&p_full[t]);
+      l_run += (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y);
     }
-    if (ok && mbar_wait(o_full, (nb - 1) & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+    if (ok && mbar_wait(&o_full[t], (nb - 1) & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
       float o[64];
       const float inv = 1.0f / l_run;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t r0[32];
-        tmem_ld32(tmem + lane_base + COL_O + h * 32, r0);
+        tmem_ld32(tb + lane_base + COL_O + h * 32, r0);
         tmem_wait_ld();
 #pragma unroll
         for (int d = 0; d < 32; ++d) o[h * 32 + d] = __uint_as_float(r0[d]) * inv;
@@ -239,6 +263,7 @@ __global__ void __launch_bounds__(A_THREADS, 2)
             dst[d] = make_uint4(pack_bf16x2(o[8 * d], o[8 * d + 1]), pack_bf16x2(o[8 * d + 2], o[8 * d + 3]),
                                 pack_bf16x2(o[8 * d + 4], o[8 * d + 5]), pack_bf16x2(o[8 * d + 6], o[8 * d + 7]));
         } else {
+          // two Q8_0 blocks of 32 dims (quantize_row_q8_0, src/q8_0_dot.rs:34-45)
           const size_t row = static_cast<size_t>(b_img) * tokens + qrow;
           int8_t* dst = static_cast<int8_t*>(out) + row * (heads * 64) + h * 64;
 #pragma unroll
@@ -253,9 +278,9 @@ __global__ void __launch_bounds__(A_THREADS, 2)
             for (int q = 0; q < 8; ++q) {
               uint32_t packed = 0;
 #pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                const float qf = fminf(fmaxf(roundf(o[blk * 32 + 4 * q + t] * id), -127.0f), 127.0f);
-                packed |= (static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xffu) << (8 * t);
+              for (int u = 0; u < 4; ++u) {
+                const float qf = fminf(fmaxf(roundf(o[blk * 32 + 4 * q + u] * id), -127.0f), 127.0f);
+                packed |= (static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xffu) << (8 * u);
               }
               w[q] = packed;
             }
@@ -271,7 +296,7 @@ __global__ void __launch_bounds__(A_THREADS, 2)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -285,7 +310,7 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  dim3 grid((tokens + AQ - 1) / AQ, images * heads);
+  dim3 grid((tokens + 2 * AQ - 1) / (2 * AQ), images * heads);
   k_attention_tc<OUT><<<grid, A_THREADS, ATT_SMEM, s>>>(mq, mk, mv, heads, tokens, out, q8d, err);
   return cudaGetLastError();
 }
