@@ -190,6 +190,7 @@ def run_vestra(args, rank, world, local_rank):
     import torch
 
     import vestra_kernels as vk
+    from vestra_kernels.sharding import max_over_ranks
 
     torch.cuda.set_device(local_rank)
     math = {"bf16": vk.MATH_BF16, "q8": vk.MATH_Q8_0, "f32": vk.MATH_F32}[args.math]
@@ -245,10 +246,7 @@ def run_vestra(args, rank, world, local_rank):
     # per-kernel device time (eager forward with events between kernels)
     slots = enc.profile(x, out, B, gh, gw)
 
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), float(t[1])
+    ms, e2e_ms = max_over_ranks(ms), max_over_ranks(e2e_ms)
     if rank != 0:
         return
 
@@ -273,7 +271,8 @@ def run_vestra(args, rank, world, local_rank):
                                f"({T} tokens), random-init weights, tokens ~N(0,1)",
                    "images_per_gpu": B, "global_batch": images, "tokens": T, "layers": LAYERS,
                    "math": args.math, "parallelism": f"image-sharded x{world}, no collective",
-                   "l2": "inputs larger than L2 (activations 170 MB per step)"},
+                   "l2": "working set larger than L2: %.0f MB of activations per layer (126 MB L2)"
+                         % (B * T * (E * 4 + 5 * E * 2 + F * 2) / 1e6)},
         "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": int(hin.numel() * 4),
                 "d2h_bytes_per_step": int(hout.numel() * 4)},
         "gpu_launches": launches,

@@ -86,6 +86,14 @@ def test_gemm_q8_0_rejects_unsupported_shape(vk, ctx):
     assert float(c.abs().sum()) == 0.0
 
 
+def test_gemm_q8_0_empty_is_a_no_op(vk, ctx):
+    z = torch.zeros(34 * 4, dtype=torch.uint8, device="cuda")
+    c = torch.full((8,), 7.0, device="cuda")
+    assert vk.gemm_q8_0(0, 128, 128, z, z, c, ctx=ctx)
+    assert vk.gemm_q8_0(1, 0, 128, z, z, c, ctx=ctx)
+    assert float(c.sum()) == 56.0
+
+
 # ---------------------------------------------------------------- projections
 SHAPES = [(768, 2304), (768, 768), (768, 3072), (3072, 768)]
 
