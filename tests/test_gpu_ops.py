@@ -241,6 +241,27 @@ def test_flash_attention_bf16(vk, ctx, oracle_lib, tokens, heads):
         ctx.set_math(vk.MATH_F32)
 
 
+@pytest.mark.parametrize("boost", [1.0, 40.0, 400.0])
+def test_flash_attention_bf16_logit_jumps(vk, ctx, oracle_lib, boost):
+    """Keys in a late block whose logits exceed every earlier one by far (up
+    to ~3000 in score units): the online softmax must re-reference its
+    running maximum without overflowing."""
+    ctx.set_math(vk.MATH_BF16)
+    try:
+        heads, tokens = 2, 865
+        q, k, v = rng_inputs(91, *[(heads, tokens, 64)] * 3)
+        k[:, 600:610] *= np.float32(boost)
+        q, k, v = (oracle_lib.round_bf16(t) for t in (q, k, v))
+        out = torch.empty(q.size, device="cuda")
+        assert vk.flash_attention_f32_da3_base(dev(q), dev(k), dev(v), heads, tokens, out, ctx=ctx)
+        got = host(out).reshape(q.shape)
+        assert np.isfinite(got).all()
+        err = rel_l2(got, oracle_lib.attention_naive(q, k, v))
+        assert err < 2e-3, err
+    finally:
+        ctx.set_math(vk.MATH_F32)
+
+
 # ---------------------------------------------------------------- norms, RoPE, pointwise
 @pytest.mark.parametrize("rows,cols", [(865, 768), (67, 64), (5, 100)])
 def test_layernorm(vk, ctx, oracle_lib, rows, cols):
