@@ -5,26 +5,25 @@
 // path (src/specialized.rs:730-765, 1400-1562; src/attention.rs:111-201):
 // non-causal softmax(Q K^T / 8) V with an online softmax over key blocks.
 //
-// One CTA per SM handles up to four 128-query tiles of one (image, head):
-// every K/V block of 64 keys is loaded once for 512 queries, and the four
-// tiles' softmax chains (S -> registers -> P -> O) interleave, so the tensor
-// core and the MUFU unit always have another tile's work while one tile
-// waits for its MMAs.
+// One CTA per SM handles two 128-query tiles (A and B) of one (image, head)
+// so every K/V block is loaded once for 256 queries and the two tiles
+// ping-pong on the tensor core: while the softmax warps of A work on S_A(j),
+// the tensor core computes S_B(j), O_A(j-1) and S_A(j+1).
 //
-//   warp 0       TMA: the Q tiles once, then K and V blocks of 64 keys
-//                (AST-stage ring shared by all tiles)
-//   warp 1       TMEM owner; one lane issues, per key block j and tile t,
-//                  O_t  += P_t(j) V_j      (M=128, N=64, K=64; A = P_t from TMEM)
-//                  S_t(j+1) = Q_t K_j+1^T   (M=128, N=64, K=64; A, B from smem)
-//                both into tile t's TMEM; the tensor core runs them in issue
-//                order, so S_t(j+1) overwrites P_t(j) only after O_t read it
-//   warps 2..17  softmax, four warps per tile, one query row per thread: the
-//                64 scores of a block in registers, block max, p =
-//                2^(s*log2e/8 - m_ref), row sum, P -> TMEM as bf16 over S.
-//                O accumulates in TMEM; it is rescaled only when the block max
-//                passes m_ref by more than 2^8.  Finally O / l is stored
-//                token-major bf16 / Q8_0 or head-major f32.
-// TMEM per tile (128 columns): S / P [0, 64), O [64, 128).
+//   warp 0      TMA: the two Q tiles once, then K and V blocks of 128 keys
+//               (AST-stage ring shared by both tiles)
+//   warp 1      TMEM owner; one lane issues, per tile t and key block j,
+//                 S_t(j) = Q_t K_j^T     (M=128, N=128, K=64; A, B from smem)
+//                 O_t   += P_t(j) V_j     (M=128, N=64, K=128; A = P_t from TMEM)
+//   warps 2..5  softmax of tile A, warps 6..9 of tile B, one query row per
+//               thread: two passes over S in TMEM (block max, then
+//               p = 2^(s*log2e/8 - m_ref), row sum, P -> TMEM as bf16), 32
+//               columns at a time so nothing spills; the other tile keeps the
+//               tensor core busy while this one holds its S.  O
+//               accumulates in TMEM; it is rescaled only when the block max
+//               passes m_ref by more than 2^8.  Finally O / l is stored
+//               token-major bf16 / Q8_0 or head-major f32.
+// TMEM per tile: S [0,128), P [128,192) (bf16 pairs), O [192,256); tile B at +256.
 #include "vk_common.cuh"
 #include "vk_internal.h"
 
@@ -32,14 +31,12 @@ namespace vk {
 
 namespace {
 constexpr int AQ = 128;        // queries per tile
-constexpr int NT = 4;          // tiles per CTA
-constexpr int AKV = 64;        // keys per block
-constexpr int AST = 6;         // K/V pipeline stages
-constexpr int A_THREADS = 64 + NT * 128;  // producer, MMA, 4 softmax warps per tile
-constexpr int Q_BYTES = AQ * 128;         // 128 rows x 64 bf16
-constexpr int KV_BYTES = AKV * 128;       // 64 rows x 64 bf16
-constexpr uint32_t COL_O = 64, TILE_COLS = 128;
-constexpr size_t ATT_SMEM = 1024 + Q_BYTES * NT + 2 * KV_BYTES * AST + 256;
+constexpr int AKV = 128;       // keys per block
+constexpr int AST = 4;         // K/V pipeline stages
+constexpr int A_THREADS = 320; // producer, MMA, 2 x 4 softmax warps
+constexpr int TILE_BYTES = 128 * 128;  // 128 rows x 64 bf16
+constexpr uint32_t COL_S = 0, COL_O = 128, TILE_COLS = 256;  // S / P [0, 128), O [128, 192)
+constexpr size_t ATT_SMEM = 1024 + TILE_BYTES * (2 + 2 * AST) + 256;
 }  // namespace
 
 template <int OUT>
@@ -49,22 +46,22 @@ __global__ void __launch_bounds__(A_THREADS, 1)
                    int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;  // NT tiles
-  uint8_t* sK = sQ + NT * Q_BYTES;
-  uint8_t* sV = sK + AST * KV_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + AST * KV_BYTES);
+  uint8_t* sQ = smem;  // tile A, then tile B
+  uint8_t* sK = smem + 2 * TILE_BYTES;
+  uint8_t* sV = sK + AST * TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + AST * TILE_BYTES);
   uint64_t* q_full = bars;
   uint64_t* kv_full = q_full + 1;
   uint64_t* kv_empty = kv_full + AST;
-  uint64_t* s_full = kv_empty + AST;  // [NT] S_t(j) ready (and O_t(j-1) done)
-  uint64_t* p_full = s_full + NT;     // [NT] P_t(j) written
-  uint64_t* o_done = p_full + NT;     // [NT] last O_t finished
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + NT);
+  uint64_t* s_full = kv_empty + AST;  // [2]
+  uint64_t* p_full = s_full + 2;      // [2]
+  uint64_t* o_full = p_full + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
-  const int q0 = blockIdx.x * NT * AQ;
-  const int ntiles = min(NT, (tokens - q0 + AQ - 1) / AQ);
+  const int q0 = blockIdx.x * 2 * AQ;
+  const int ntiles = (tokens - q0 > AQ) ? 2 : 1;  // tile B may not exist
   const int nb = (tokens + AKV - 1) / AKV;
 
   if (threadIdx.x == 0) {
@@ -73,10 +70,10 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int t = 0; t < NT; ++t) {
+    for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 128);
-      mbar_init(&o_done[t], 1);
+      mbar_init(&o_full[t], 1);
     }
     fence_mbar_init();
   }
@@ -91,27 +88,29 @@ __global__ void __launch_bounds__(A_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, ntiles * Q_BYTES);
-      for (int t = 0; t < ntiles; ++t) tma_load_3d(sQ + t * Q_BYTES, &tmQ, q_full, 0, q0 + t * AQ, bh);
+      mbar_arrive_expect_tx(q_full, ntiles * TILE_BYTES);
+      for (int t = 0; t < ntiles; ++t) tma_load_3d(sQ + t * TILE_BYTES, &tmQ, q_full, 0, q0 + t * AQ, bh);
       for (int j = 0; j < nb; ++j) {
         const int st = j % AST;
         if (!mbar_wait(&kv_empty[st], ((j / AST) & 1) ^ 1, err, VK_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * KV_BYTES);
-        tma_load_3d(sK + st * KV_BYTES, &tmK, &kv_full[st], 0, j * AKV, bh);
-        tma_load_3d(sV + st * KV_BYTES, &tmV, &kv_full[st], 0, j * AKV, bh);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        tma_load_3d(sK + st * TILE_BYTES, &tmK, &kv_full[st], 0, j * AKV, bh);
+        tma_load_3d(sV + st * TILE_BYTES, &tmV, &kv_full[st], 0, j * AKV, bh);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idS = idesc_bf16(128, AKV);
+      constexpr uint32_t idS = idesc_bf16(128, 128);
       constexpr uint32_t idO = idesc_bf16_bmn(128, 64);
-      auto issue_s = [&](int t, int j) {  // K_j resident, P_t(j-1) consumed by an earlier MMA
-        const uint64_t qdesc = smem_desc_k_sw128(smem_u32(sQ + t * Q_BYTES));
-        const uint64_t kdesc = smem_desc_k_sw128(smem_u32(sK + (j % AST) * KV_BYTES));
+      // S_t(j) into tile t's S / P columns; the tensor core runs MMAs in
+      // issue order, so it overwrites P_t(j-1) only after O_t(j-1) read it
+      auto issue_s = [&](int t, int j) {
+        const uint64_t qdesc = smem_desc_k_sw128(smem_u32(sQ + t * TILE_BYTES));
+        const uint64_t kdesc = smem_desc_k_sw128(smem_u32(sK + (j % AST) * TILE_BYTES));
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_f16(tmem + t * TILE_COLS, qdesc + static_cast<uint64_t>(k * 2), kdesc + static_cast<uint64_t>(k * 2),
-                   idS, k > 0 ? 1u : 0u);
+          umma_f16(tmem + t * TILE_COLS + COL_S, qdesc + static_cast<uint64_t>(k * 2),
+                   kdesc + static_cast<uint64_t>(k * 2), idS, k > 0 ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, err, VK_DEV_TIMEOUT_MMA) && mbar_wait(&kv_full[0], 0, err, VK_DEV_TIMEOUT_MMA);
       if (ok) {
@@ -124,20 +123,20 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       for (int j = 0; j < nb && ok; ++j) {
         const bool more = j + 1 < nb;
         if (more && !(ok = mbar_wait(&kv_full[(j + 1) % AST], ((j + 1) / AST) & 1, err, VK_DEV_TIMEOUT_MMA))) break;
-        const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(sV + (j % AST) * KV_BYTES));
+        const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(sV + (j % AST) * TILE_BYTES));
         for (int t = 0; t < ntiles && ok; ++t) {
           if (!(ok = mbar_wait(&p_full[t], j & 1, err, VK_DEV_TIMEOUT_MMA))) break;
           tc_fence_after();
           const uint32_t base = tmem + t * TILE_COLS;
 #pragma unroll
           for (int k = 0; k < AKV / 16; ++k)
-            umma_f16_ts(base + COL_O, base + static_cast<uint32_t>(k * 8),
+            umma_f16_ts(base + COL_O, base + COL_S + static_cast<uint32_t>(k * 8),
                         vdesc + static_cast<uint64_t>(k * (2048 >> 4)), idO, (j | k) > 0 ? 1u : 0u);
           if (more) {
             issue_s(t, j + 1);
-            umma_commit(&s_full[t]);
+            umma_commit(&s_full[t]);  // also covers O_t(j)
           } else {
-            umma_commit(&o_done[t]);
+            umma_commit(&o_full[t]);
           }
         }
         if (ok) umma_commit(&kv_empty[j % AST]);  // after every MMA that read stage j
@@ -159,76 +158,97 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         break;
       }
       tc_fence_after();
-      uint32_t r[64];
-      tmem_ld32(tb, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      tmem_ld32(tb + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      tmem_wait_ld();
       const int valid = tokens - j * AKV;
       const bool full_block = valid >= AKV;
-      float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (full_block) {
+      // block max over S(j), 32 TMEM columns at a time
+      auto block_max = [&]() -> float {
+        float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int i = 0; i < 64; i += 2)
-          pm[(i >> 1) & 3] = max3f(pm[(i >> 1) & 3], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-      } else {
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tb + COL_S + c * 32, r);
+          tmem_wait_ld();
+          if (full_block) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (i < valid) pm[i & 3] = fmaxf(pm[i & 3], __uint_as_float(r[i]));
-      }
-      const float m_blk = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])) * sl2;
-      bool rescale = false;
-      float f = 1.0f;
-      if (j == 0) {
-        m_ref = m_blk;
-      } else if (m_blk > m_ref + 8.0f) {
-        rescale = true;
-        f = ex2_approx(m_ref - m_blk);
-        m_ref = m_blk;
-      }
-      // probabilities -> P (bf16 pairs, packed in place into r[0..31] and
-      // stored over the first 32 columns of S), row sum
-      float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-      const float2 scale2 = make_float2(sl2, sl2), shift2 = make_float2(-m_ref, -m_ref);
+            for (int i = 0; i < 32; i += 2)
+              pm[(i >> 1) & 3] = max3f(pm[(i >> 1) & 3], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+          } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float2 x = ffma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), scale2, shift2);
-        float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-        if (!full_block) {
-          pp.x = 2 * i < valid ? pp.x : 0.0f;
-          pp.y = 2 * i + 1 < valid ? pp.y : 0.0f;
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i < valid) pm[i & 3] = fmaxf(pm[i & 3], __uint_as_float(r[i]));
+          }
         }
-        ps[i & 1] = fadd2(ps[i & 1], pp);
-        r[i] = pack_bf16x2(pp.x, pp.y);
-      }
-      tmem_st32(tb, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      if (__any_sync(0xffffffffu, rescale)) {  // TMEM access is warp-collective
-        // O_t(j-1) is complete (S_t(j) was issued after it) and O_t(j) has
-        // not started (it waits for p_full): bring O to the new reference
-        uint32_t* o = &r[32];
+        return fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])) * sl2;
+      };
+      // p = 2^(s * log2e / 8 - m) packed as bf16 pairs into pk; returns the row sum
+      uint32_t pk[64];
+      auto exp_pass = [&](float m) -> float {
+        float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+        const float2 scale2 = make_float2(sl2, sl2), shift2 = make_float2(-m, -m);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tb + COL_S + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k0 = c * 32 + 2 * i;
+            const float2 x = ffma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), scale2, shift2);
+            float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            if (!full_block) {
+              pp.x = k0 < valid ? pp.x : 0.0f;
+              pp.y = k0 + 1 < valid ? pp.y : 0.0f;
+            }
+            ps[i & 1] = fadd2(ps[i & 1], pp);
+            pk[c * 16 + i] = pack_bf16x2(pp.x, pp.y);
+          }
+        }
+        return (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y);
+      };
+      if (j == 0) m_ref = block_max();
+      // One pass against the running reference m_ref (the max of block 0, or
+      // of a later block that outgrew it).  Probabilities above 1 are fine:
+      // the final O / l is invariant to the reference, and f32 / bf16 hold
+      // p up to 2^127.  Only when a row's block sum passes 2^64 is the block
+      // redone against its own max, with O and l rescaled to match (O_t(j-1)
+      // is complete: S_t(j) was issued after it).
+      float l_blk = exp_pass(m_ref);
+      if (j > 0 && __any_sync(0xffffffffu, !(l_blk < 18446744073709551616.0f))) {  // TMEM access is warp-collective
+        const float m_new = fmaxf(m_ref, block_max());
+        const float f = ex2_approx(m_ref - m_new);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          tmem_ld32(tb + COL_O + h * 32, *reinterpret_cast<uint32_t(*)[32]>(o));
+          uint32_t o[32];
+          tmem_ld32(tb + COL_O + h * 32, o);
           tmem_wait_ld();
 #pragma unroll
           for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * f);
-          tmem_st32(tb + COL_O + h * 32, *reinterpret_cast<uint32_t(*)[32]>(o));
+          tmem_st32(tb + COL_O + h * 32, o);
         }
         l_run *= f;
+        m_ref = m_new;
+        l_blk = exp_pass(m_ref);
       }
+      // P over the first 64 columns of S (S is no longer needed)
+      tmem_st32(tb + COL_S, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+      tmem_st32(tb + COL_S + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
-      l_run += (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y);
+      l_run += l_blk;
     }
-    if (ok && mbar_wait(&o_done[t], 0, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+    if (ok && mbar_wait(&o_full[t], 0, err, VK_DEV_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
       float o[64];
       const float inv = 1.0f / l_run;
-      tmem_ld32(tb + COL_O, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-      tmem_ld32(tb + COL_O + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
-      tmem_wait_ld();
 #pragma unroll
-      for (int d = 0; d < 64; ++d) o[d] *= inv;
+      for (int h = 0; h < 2; ++h) {
+        uint32_t r0[32];
+        tmem_ld32(tb + COL_O + h * 32, r0);
+        tmem_wait_ld();
+#pragma unroll
+        for (int d = 0; d < 32; ++d) o[h * 32 + d] = __uint_as_float(r0[d]) * inv;
+      }
       if (qrow < tokens) {
         const int b_img = bh / heads, h = bh - b_img * heads;
         if constexpr (OUT == ATTN_OUT_HEAD_F32) {
@@ -290,7 +310,7 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  dim3 grid((tokens + NT * AQ - 1) / (NT * AQ), images * heads);
+  dim3 grid((tokens + 2 * AQ - 1) / (2 * AQ), images * heads);
   k_attention_tc<OUT><<<grid, A_THREADS, ATT_SMEM, s>>>(mq, mk, mv, heads, tokens, out, q8d, err);
   return cudaGetLastError();
 }
@@ -303,9 +323,9 @@ cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const
   const uint64_t bh = static_cast<uint64_t>(images) * heads;
   const void* bases[3] = {q, k, v};
   CUtensorMap* maps[3] = {&mq, &mk, &mv};
-  for (int i = 0; i < 3; ++i)  // Q boxes of 128 rows, K / V boxes of AKV rows
+  for (int i = 0; i < 3; ++i)
     if (!make_tmap_3d(maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, bases[i], 64, tokens, bh, 128,
-                      static_cast<uint64_t>(tokens) * 128, 64, i == 0 ? AQ : AKV, CU_TENSOR_MAP_SWIZZLE_128B))
+                      static_cast<uint64_t>(tokens) * 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
   switch (out_mode) {
     case ATTN_OUT_HEAD_F32: return launch_attn<ATTN_OUT_HEAD_F32>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
