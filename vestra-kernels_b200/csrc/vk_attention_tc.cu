@@ -35,6 +35,12 @@ constexpr int AKV = 128;       // keys per block
 constexpr int AST = 4;         // K/V pipeline stages
 constexpr int A_THREADS = 320; // producer, MMA, 2 x 4 softmax warps
 constexpr int TILE_BYTES = 128 * 128;  // 128 rows x 64 bf16
+// Pairs i (of the 16 per 32-column chunk) whose exponentials use the
+// FMA-pipe polynomial instead of MUFU ex2 (16 lanes per clock per SM).
+#ifndef VK_ATT_POLY_MASK
+#define VK_ATT_POLY_MASK 0x2929u
+#endif
+constexpr uint32_t POLY_MASK = VK_ATT_POLY_MASK;
 constexpr uint32_t COL_S = 0, COL_O = 128, TILE_COLS = 256;  // S / P [0, 128), O [128, 192)
 constexpr size_t ATT_SMEM = 1024 + TILE_BYTES * (2 + 2 * AST) + 256;
 }  // namespace
@@ -194,7 +200,8 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           for (int i = 0; i < 16; ++i) {
             const int k0 = c * 32 + 2 * i;
             const float2 x = ffma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), scale2, shift2);
-            float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            float2 pp = ((POLY_MASK >> i) & 1) ? exp2_poly2(x)                                  // FMA pipe
+                                               : make_float2(ex2_approx(x.x), ex2_approx(x.y));  // MUFU
             if (!full_block) {
               pp.x = k0 < valid ? pp.x : 0.0f;
               pp.y = k0 + 1 < valid ? pp.y : 0.0f;

@@ -47,9 +47,12 @@ struct Cfg {
   static constexpr int WARP_COLS = TILE_N / 2;     // columns one epilogue warp handles
   static constexpr int STAGE_BYTES = 2 * SLAB_BYTES;
   static constexpr int OUT_BUF = F32OUT ? 4096 : 2048;  // 32 x 32 staging tile
-  static constexpr int OUT_BYTES = 8 * 2 * OUT_BUF;     // 8 warps, double buffered
+  // f32 outputs: two 32 x 32 tiles per warp, double buffered chunk by chunk;
+  // bf16 outputs: the warp's whole 32 x WARP_COLS slice, one fence per tile
+  static constexpr int WARP_BUFS = F32OUT ? 2 : (WARP_COLS / 32 > 2 ? WARP_COLS / 32 : 2);
+  static constexpr int OUT_BYTES = 8 * WARP_BUFS * OUT_BUF;
   static constexpr int BIAS_BYTES = 2 * TILE_N * 4;     // bias + scale of the tile
-  static constexpr int STAGES = F32OUT ? 4 : 5;
+  static constexpr int STAGES = (F32OUT || PAIR) ? 4 : 5;
   static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + OUT_BYTES + BIAS_BYTES + 256;
   static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -78,6 +81,23 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const float (&
 }
 }  // namespace
 
+// TMA store (or reduce-add) of one staged 32 x 32 chunk at rows
+// [row0, row0 + 32), columns [col0, col0 + 32).
+template <int MODE>
+__device__ __forceinline__ void store_chunk(const GemmEpi& epi, const CUtensorMap* tmO0, const CUtensorMap* tmO1,
+                                            const CUtensorMap* tmO2, uint8_t* buf, int row0, int col0, int img,
+                                            int t0) {
+  if constexpr (MODE == EPI_RESID) {
+    tma_reduce_add_2d(tmO0, buf, col0, row0);
+  } else if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32) {
+    const QkvPos q = qkv_pos(epi, row0, col0);
+    const CUtensorMap* map = q.g == 0 ? tmO0 : (q.g == 1 ? tmO1 : tmO2);
+    tma_store_3d(map, buf, q.axis * 32, t0, img * epi.heads + q.head);
+  } else {
+    tma_store_2d(tmO0, buf, col0, row0);
+  }
+}
+
 // Epilogue of one warp's share of an accumulator tile: rows [row0, row0+32),
 // columns [c0, c0 + NCOL).  `release` runs once the TMEM columns have all
 // been read (it hands the accumulator back to the MMA warp).
@@ -98,6 +118,14 @@ __device__ __forceinline__ void epilogue_part(const GemmEpi& epi, const CUtensor
     t0 = row0 - img * epi.tokens;
     direct = (t0 + 32 > epi.tokens) || (row0 + 32 > M);
   }
+  // bf16 outputs stage every chunk of the slice (buffer c) and publish them
+  // with one proxy fence; f32 outputs alternate two buffers chunk by chunk.
+  constexpr bool GROUPED = !F32;
+  bool staged = false;
+  if constexpr (GROUPED) {
+    if (lane == 0) bulk_wait_read<0>();  // the previous tile's stores are done with the slice
+    __syncwarp();
+  }
   uint32_t r[2][32];
   tmem_ld32(tbase, r[0]);
 #pragma unroll
@@ -117,6 +145,11 @@ __device__ __forceinline__ void epilogue_part(const GemmEpi& epi, const CUtensor
       if (row < M) epi_direct<MODE>(epi, row, col0, N, v);
       continue;
     }
+    if constexpr (GROUPED) {
+      stage_row<F32>(stage + c * OUT_BUF, lane, v);
+      staged = true;
+      continue;
+    }
     uint8_t* buf = stage + sb * OUT_BUF;
     if (lane == 0) bulk_wait_read<1>();  // the store that last read `buf` is done with it
     __syncwarp();
@@ -124,18 +157,21 @@ __device__ __forceinline__ void epilogue_part(const GemmEpi& epi, const CUtensor
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) {
-      if constexpr (MODE == EPI_RESID) {
-        tma_reduce_add_2d(tmO0, buf, col0, row0);
-      } else if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32) {
-        const QkvPos q = qkv_pos(epi, row0, col0);
-        const CUtensorMap* map = q.g == 0 ? tmO0 : (q.g == 1 ? tmO1 : tmO2);
-        tma_store_3d(map, buf, q.axis * 32, t0, img * epi.heads + q.head);
-      } else {
-        tma_store_2d(tmO0, buf, col0, row0);
-      }
+      store_chunk<MODE>(epi, tmO0, tmO1, tmO2, buf, row0, col0, img, t0);
       bulk_commit();
     }
     sb ^= 1;
+  }
+  if constexpr (GROUPED) {
+    if (staged) {
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+#pragma unroll
+        for (int c = 0; c < NCOL / 32; ++c) store_chunk<MODE>(epi, tmO0, tmO1, tmO2, stage + c * OUT_BUF, row0, c0 + c * 32, img, t0);
+        bulk_commit();
+      }
+    }
   }
 }
 
@@ -275,7 +311,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int quad = warp & 3;      // TMEM lanes [32*quad, 32*quad + 32) are this warp's
     const int chalf = ew >> 2;      // which half of the tile's columns
     const int et = threadIdx.x - 64;
-    uint8_t* stage = sOut + ew * 2 * C::OUT_BUF;
+    uint8_t* stage = sOut + ew * C::WARP_BUFS * C::OUT_BUF;
     int sb = 0;
     int it = 0;
     bool ok = true;
