@@ -9,7 +9,7 @@ GPU (random-init weights W~N(0,0.02), b~N(0,0.01), LayerScale 1e-5; tokens
 under torchrun every rank runs its own shard (weak scaling, no collective);
 time is the max over ranks of CUDA-event time around K steps.
 
-`e2e` is the same metric through vk_encoder_forward_host: pinned host tokens
+`e2e` is the same metric through vk_encoder_forward_host_async: pinned host tokens
 in, host result out, copies pipelined with the compute inside the timed
 region.  `--impl reference` times the reference's CPU fast path (the
 AVX-512 restatement in oracle/, all host cores) on rank 0.
@@ -238,7 +238,7 @@ def run_vestra(args, rank, world, local_rank):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        enc.forward_host(hin, hout, B, gh, gw)
+        enc.forward_host_async(hin, hout, B, gh, gw)  # every step copies its tokens in and its result out
     e1.record()
     barrier()
     e2e_ms = e0.elapsed_time(e1)

@@ -197,6 +197,15 @@ int vk_encoder_forward(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_
  * compute in image chunks (the end-to-end entry point). */
 int vk_encoder_forward_host(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h,
                             size_t grid_w, const float* tokens_host, float* out_host);
+/* As vk_encoder_forward_host but returns once the work is enqueued: the
+ * result is in out_host after vk_synchronize(ctx) (or any later work on the
+ * context stream).  Back-to-back calls overlap one call's copies with the
+ * neighbouring calls' compute.  Both host buffers must stay valid and
+ * tokens_host unmodified until then; pinned host memory is needed for the
+ * copies to overlap.  Work enqueued on the context stream before the call is
+ * not waited for (vk_synchronize first if it must be). */
+int vk_encoder_forward_host_async(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h,
+                                  size_t grid_w, const float* tokens_host, float* out_host);
 /* One eager forward with CUDA events between kernels: ms_per_slot[i] sums
  * the device time of the i-th kernel of every block (slots >= 7 for bf16 /
  * Q8_0, >= 10 for f32; order as in the block description above). */

@@ -126,6 +126,19 @@ def test_graph_replay_and_host_path_match(vk, ctx, oracle_lib):
         for _ in range(2):
             enc.forward_host(hin, hout, 5, gh, gw)
             assert np.array_equal(hout.numpy(), outs[0])
+        # back-to-back asynchronous calls on different buffers, interleaved
+        # with a device-path forward, all ordered through the shared ring
+        hin2 = torch.from_numpy(x[::-1].copy()).pin_memory()
+        hout2 = torch.empty_like(hin2).pin_memory()
+        hout.zero_()
+        enc.forward_host_async(hin, hout, 5, gh, gw)
+        enc.forward_host_async(hin2, hout2, 5, gh, gw)
+        o = torch.empty_like(t)
+        enc.forward(t, o, 5, gh, gw)
+        ctx.synchronize()
+        assert np.array_equal(hout.numpy(), outs[0])
+        assert np.array_equal(hout2.numpy(), outs[0][::-1])
+        assert np.array_equal(o.cpu().numpy(), outs[0])
     finally:
         del os.environ["VK_E2E_CHUNK"]
 

@@ -72,9 +72,16 @@ struct vk_encoder {
   std::map<std::tuple<size_t, size_t, size_t, const void*, void*, cudaStream_t>, int> seen;
   int last_launches = 0;
   // end-to-end pipeline resources
+  // (three device slots of image chunks cycle H2D -> compute -> D2H; the
+  // ring and its events persist across calls so consecutive calls overlap)
   cudaStream_t h2d = nullptr, d2h = nullptr, comp = nullptr;
   float* slots[3] = {nullptr, nullptr, nullptr};
+  cudaEvent_t slot_free[3] = {nullptr, nullptr, nullptr};  // D2H out of the slot finished
+  cudaEvent_t slot_in[3] = {nullptr, nullptr, nullptr};    // H2D into the slot finished
+  cudaEvent_t slot_out[3] = {nullptr, nullptr, nullptr};   // compute on the slot finished
+  cudaEvent_t dev_tail = nullptr;  // last use of the activations from the context stream
   size_t slot_rows = 0;
+  size_t next_slot = 0;
 };
 
 int vk_fail(int status, const char* fmt, ...);

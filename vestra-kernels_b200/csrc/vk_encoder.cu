@@ -216,6 +216,10 @@ void free_encoder(vk_encoder* enc) {
     if (p) cudaFree(p);
   for (cudaStream_t st : {enc->h2d, enc->d2h, enc->comp})
     if (st) cudaStreamDestroy(st);
+  for (int i = 0; i < 3; ++i)
+    for (cudaEvent_t ev : {enc->slot_free[i], enc->slot_in[i], enc->slot_out[i]})
+      if (ev) cudaEventDestroy(ev);
+  if (enc->dev_tail) cudaEventDestroy(enc->dev_tail);
   delete enc;
 }
 
@@ -333,25 +337,42 @@ extern "C" int vk_encoder_forward(vk_ctx* ctx, vk_encoder* enc, size_t images, s
   cudaSetDevice(ctx->device);
   if (images == 0) return VK_OK;
   if (grid_h == 0 || grid_w == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_forward: empty patch grid");
-  return forward_on_stream(ctx, enc, images, grid_h, grid_w, tokens_dev, out_dev, ctx->stream);
+  // after any host-pipeline compute still using the shared activations
+  if (enc->comp) {
+    for (cudaEvent_t ev : enc->slot_out)
+      if (ev) VK_TRY_CUDA(cudaStreamWaitEvent(ctx->stream, ev, 0), "vk_encoder_forward ordering");
+  }
+  VK_TRY(forward_on_stream(ctx, enc, images, grid_h, grid_w, tokens_dev, out_dev, ctx->stream));
+  if (enc->dev_tail) VK_TRY_CUDA(cudaEventRecord(enc->dev_tail, ctx->stream), "vk_encoder_forward ordering");
+  return VK_OK;
 }
 
-extern "C" int vk_encoder_forward_host(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h, size_t grid_w,
-                                       const float* tokens_host, float* out_host) {
-  if (!ctx || !enc || !tokens_host || !out_host)
-    return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_forward_host: NULL argument");
+// Host tokens in, host result out, in chunks of `chunk` images through the
+// three-slot ring: H2D on one stream, the encoder on another, D2H on a
+// third, so the copies of one chunk overlap the compute of its neighbours.
+// The ring continues across calls, so back-to-back calls overlap too.
+static int host_pipeline(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h, size_t grid_w,
+                         const float* tokens_host, float* out_host, bool wait, const char* name) {
+  if (!ctx || !enc || !tokens_host || !out_host) return vk_fail(VK_ERR_INVALID_ARGUMENT, "%s: NULL argument", name);
   cudaSetDevice(ctx->device);
   if (images == 0) return VK_OK;
-  if (grid_h == 0 || grid_w == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_forward_host: empty patch grid");
+  if (grid_h == 0 || grid_w == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "%s: empty patch grid", name);
   const size_t T = grid_h * grid_w + 1, E = enc->embed;
-  size_t chunk = 16;
+  // A waiting call overlaps copies with compute only inside itself, so it
+  // cuts the batch into 16-image chunks; back-to-back asynchronous calls
+  // overlap with each other, so each takes its batch whole (up to 64 images,
+  // where the GEMMs already fill the GPU), which keeps every GEMM large.
+  size_t chunk = wait ? 16 : 64;
   if (const char* c = getenv("VK_E2E_CHUNK")) chunk = static_cast<size_t>(atoi(c));
   if (chunk == 0 || chunk > images) chunk = images;
   const size_t rows = chunk * T;
   if (!enc->comp) {
-    VK_TRY_CUDA(cudaStreamCreateWithFlags(&enc->comp, cudaStreamNonBlocking), "pipeline stream");
-    VK_TRY_CUDA(cudaStreamCreateWithFlags(&enc->h2d, cudaStreamNonBlocking), "pipeline stream");
-    VK_TRY_CUDA(cudaStreamCreateWithFlags(&enc->d2h, cudaStreamNonBlocking), "pipeline stream");
+    for (cudaStream_t* st : {&enc->comp, &enc->h2d, &enc->d2h})
+      VK_TRY_CUDA(cudaStreamCreateWithFlags(st, cudaStreamNonBlocking), "pipeline stream");
+    for (int i = 0; i < 3; ++i)
+      for (cudaEvent_t* ev : {&enc->slot_free[i], &enc->slot_in[i], &enc->slot_out[i]})
+        VK_TRY_CUDA(cudaEventCreateWithFlags(ev, cudaEventDisableTiming), "pipeline event");
+    VK_TRY_CUDA(cudaEventCreateWithFlags(&enc->dev_tail, cudaEventDisableTiming), "pipeline event");
   }
   if (rows > enc->slot_rows) {
     cudaDeviceSynchronize();
@@ -362,40 +383,41 @@ extern "C" int vk_encoder_forward_host(vk_ctx* ctx, vk_encoder* enc, size_t imag
     for (float*& p : enc->slots) VK_TRY_CUDA(cudaMalloc(&p, rows * E * sizeof(float)), "pipeline slot");
     enc->slot_rows = rows;
   }
+  // the compute follows earlier device-path forwards on the context stream
+  VK_TRY_CUDA(cudaStreamWaitEvent(enc->comp, enc->dev_tail, 0), name);
   const size_t nchunks = (images + chunk - 1) / chunk;
-  std::vector<cudaEvent_t> ev(3 * nchunks + 1, nullptr);
-  for (auto& e : ev) VK_TRY_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "pipeline event");
-  cudaEvent_t start = ev[3 * nchunks];
-  int st = VK_OK;
-  cudaError_t e = cudaEventRecord(start, ctx->stream);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(enc->h2d, start, 0);
-  for (size_t c = 0; c < nchunks && st == VK_OK && e == cudaSuccess; ++c) {
+  size_t last = 0;
+  for (size_t c = 0; c < nchunks; ++c) {
     const size_t im0 = c * chunk, nim = (images - im0 < chunk) ? images - im0 : chunk;
-    float* slot = enc->slots[c % 3];
+    const size_t k = enc->next_slot++ % 3;
+    float* slot = enc->slots[k];
     const size_t bytes = nim * T * E * sizeof(float);
-    cudaEvent_t h2d_done = ev[3 * c], comp_done = ev[3 * c + 1], d2h_done = ev[3 * c + 2];
-    if (c >= 3) e = cudaStreamWaitEvent(enc->h2d, ev[3 * (c - 3) + 2], 0);
-    if (e == cudaSuccess)
-      e = cudaMemcpyAsync(slot, tokens_host + im0 * T * E, bytes, cudaMemcpyHostToDevice, enc->h2d);
-    if (e == cudaSuccess) e = cudaEventRecord(h2d_done, enc->h2d);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(enc->comp, h2d_done, 0);
-    if (e != cudaSuccess) break;
-    st = forward_on_stream(ctx, enc, nim, grid_h, grid_w, slot, slot, enc->comp);
-    if (st != VK_OK) break;
-    e = cudaEventRecord(comp_done, enc->comp);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(enc->d2h, comp_done, 0);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(out_host + im0 * T * E, slot, bytes, cudaMemcpyDeviceToHost, enc->d2h);
-    if (e == cudaSuccess) e = cudaEventRecord(d2h_done, enc->d2h);
+    VK_TRY_CUDA(cudaStreamWaitEvent(enc->h2d, enc->slot_free[k], 0), name);  // the slot's last D2H is done
+    VK_TRY_CUDA(cudaMemcpyAsync(slot, tokens_host + im0 * T * E, bytes, cudaMemcpyHostToDevice, enc->h2d), name);
+    VK_TRY_CUDA(cudaEventRecord(enc->slot_in[k], enc->h2d), name);
+    VK_TRY_CUDA(cudaStreamWaitEvent(enc->comp, enc->slot_in[k], 0), name);
+    VK_TRY(forward_on_stream(ctx, enc, nim, grid_h, grid_w, slot, slot, enc->comp));
+    VK_TRY_CUDA(cudaEventRecord(enc->slot_out[k], enc->comp), name);
+    VK_TRY_CUDA(cudaStreamWaitEvent(enc->d2h, enc->slot_out[k], 0), name);
+    VK_TRY_CUDA(cudaMemcpyAsync(out_host + im0 * T * E, slot, bytes, cudaMemcpyDeviceToHost, enc->d2h), name);
+    VK_TRY_CUDA(cudaEventRecord(enc->slot_free[k], enc->d2h), name);
+    last = k;
   }
-  if (st == VK_OK && e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, ev[3 * (nchunks - 1) + 2], 0);
-  cudaError_t se = cudaStreamSynchronize(enc->d2h);
-  cudaStreamSynchronize(enc->comp);
-  cudaStreamSynchronize(enc->h2d);
-  for (auto& x : ev) cudaEventDestroy(x);
-  if (st != VK_OK) return st;
-  if (e != cudaSuccess) return vk_cuda_status(e, "vk_encoder_forward_host");
-  if (se != cudaSuccess) return vk_cuda_status(se, "vk_encoder_forward_host");
+  // later work on the context stream (and vk_synchronize) sees the result
+  VK_TRY_CUDA(cudaStreamWaitEvent(ctx->stream, enc->slot_free[last], 0), name);
+  if (wait) VK_TRY_CUDA(cudaStreamSynchronize(enc->d2h), name);
   return VK_OK;
+}
+
+extern "C" int vk_encoder_forward_host(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h, size_t grid_w,
+                                       const float* tokens_host, float* out_host) {
+  return host_pipeline(ctx, enc, images, grid_h, grid_w, tokens_host, out_host, true, "vk_encoder_forward_host");
+}
+
+extern "C" int vk_encoder_forward_host_async(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h,
+                                             size_t grid_w, const float* tokens_host, float* out_host) {
+  return host_pipeline(ctx, enc, images, grid_h, grid_w, tokens_host, out_host, false,
+                       "vk_encoder_forward_host_async");
 }
 
 extern "C" int vk_encoder_profile(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_h, size_t grid_w,

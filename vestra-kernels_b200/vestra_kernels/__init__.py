@@ -72,6 +72,7 @@ SIGNATURES = {
     "vk_encoder_prepare": (_I, [_P, _P, _P, ctypes.POINTER(_P)]),
     "vk_encoder_forward": (_I, [_P, _P, _S, _S, _S, _P, _P]),
     "vk_encoder_forward_host": (_I, [_P, _P, _S, _S, _S, _P, _P]),
+    "vk_encoder_forward_host_async": (_I, [_P, _P, _S, _S, _S, _P, _P]),
     "vk_encoder_profile": (_I, [_P, _P, _S, _S, _S, _P, _P, _P, _I]),
     "vk_encoder_last_launches": (_I, [_P]),
     "vk_encoder_release": (_I, [_P]),
@@ -383,6 +384,13 @@ class Encoder:
         """Host tensors (pinned for overlap); copies are pipelined with compute."""
         _check(lib().vk_encoder_forward_host(self.ctx.handle, self.handle, images, grid_h, grid_w,
                                              ctypes.c_void_p(tokens.data_ptr()), ctypes.c_void_p(out.data_ptr())))
+
+    def forward_host_async(self, tokens, out, images: int, grid_h: int, grid_w: int) -> None:
+        """forward_host without waiting: `out` is complete after ctx.synchronize()
+        (or later work on the context stream); back-to-back calls overlap."""
+        _check(lib().vk_encoder_forward_host_async(self.ctx.handle, self.handle, images, grid_h, grid_w,
+                                                   ctypes.c_void_p(tokens.data_ptr()),
+                                                   ctypes.c_void_p(out.data_ptr())))
 
     def profile(self, tokens, out, images: int, grid_h: int, grid_w: int):
         """Per-kernel device ms of one eager forward, summed over blocks."""
