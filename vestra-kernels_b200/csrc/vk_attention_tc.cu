@@ -5,25 +5,29 @@
 // path (src/specialized.rs:730-765, 1400-1562; src/attention.rs:111-201):
 // non-causal softmax(Q K^T / 8) V with an online softmax over key blocks.
 //
-// One CTA per SM handles two 128-query tiles (A and B) of one (image, head)
-// so every K/V block is loaded once for 256 queries and the two tiles
-// ping-pong on the tensor core: while the softmax warps of A work on S_A(j),
-// the tensor core computes S_B(j), O_A(j-1) and S_A(j+1).
+// A persistent CTA per SM works through (image*head, pair of 128-query
+// tiles) items.  Every K/V block is loaded once for the item's two tiles,
+// and the tiles ping-pong on the tensor core: while the softmax warps of one
+// work on S_t(j), the tensor core runs the other tile's O += P V and next S.
+// The Q tiles and the O accumulators are double-buffered across items, so
+// the next item's loads and first MMAs overlap this item's output.
 //
-//   warp 0      TMA: the two Q tiles once, then K and V blocks of 128 keys
-//               (AST-stage ring shared by both tiles)
-//   warp 1      TMEM owner; one lane issues, per tile t and key block j,
-//                 S_t(j) = Q_t K_j^T     (M=128, N=128, K=64; A, B from smem)
-//                 O_t   += P_t(j) V_j     (M=128, N=64, K=128; A = P_t from TMEM)
-//   warps 2..5  softmax of tile A, warps 6..9 of tile B, one query row per
-//               thread: two passes over S in TMEM (block max, then
-//               p = 2^(s*log2e/8 - m_ref), row sum, P -> TMEM as bf16), 32
-//               columns at a time so nothing spills; the other tile keeps the
-//               tensor core busy while this one holds its S.  O
-//               accumulates in TMEM; it is rescaled only when the block max
-//               passes m_ref by more than 2^8.  Finally O / l is stored
-//               token-major bf16 / Q8_0 or head-major f32.
-// TMEM per tile: S [0,128), P [128,192) (bf16 pairs), O [192,256); tile B at +256.
+//   warp 0      TMA: per item the Q tiles, then K and V blocks of 128 keys
+//               (AST-stage ring running across items)
+//   warp 1      TMEM owner; one lane issues, per key block j and tile t,
+//                 O_t     += P_t(j) V_j      (M=128, N=64, K=128; A = P_t from TMEM)
+//                 S_t(j+1) = Q_t K_j+1^T     (M=128, N=128, K=64; A, B from smem)
+//               in that order: the tensor core runs MMAs in issue order, so
+//               S_t(j+1) overwrites P_t(j) only after O_t read it
+//   warps 2..5  softmax of tile 0, warps 6..9 of tile 1, one query row per
+//               thread: p = 2^(s*log2e/8 - m_ref) in one pass over S against
+//               the running reference (block 0's max), row sum, P -> TMEM as
+//               bf16 over S.  O accumulates in TMEM; a block whose row sums
+//               would overflow is redone against its own max with O
+//               rescaled.  Finally O / l is stored token-major bf16 / Q8_0 or
+//               head-major f32.
+// TMEM per tile (256 columns): S / P [0, 128), O for even / odd items
+// [128, 192) / [192, 256).
 #include "vk_common.cuh"
 #include "vk_internal.h"
 
@@ -41,45 +45,52 @@ constexpr int TILE_BYTES = 128 * 128;  // 128 rows x 64 bf16
 #define VK_ATT_POLY_MASK 0x2929u
 #endif
 constexpr uint32_t POLY_MASK = VK_ATT_POLY_MASK;
-constexpr uint32_t COL_S = 0, COL_O = 128, TILE_COLS = 256;  // S / P [0, 128), O [128, 192)
-constexpr size_t ATT_SMEM = 1024 + TILE_BYTES * (2 + 2 * AST) + 256;
+constexpr uint32_t COL_S = 0, COL_O = 128, TILE_COLS = 256;  // S / P [0, 128), O buffers [128, 192), [192, 256)
+constexpr size_t ATT_SMEM = 1024 + TILE_BYTES * (4 + 2 * AST) + 512;
 }  // namespace
 
 template <int OUT>
 __global__ void __launch_bounds__(A_THREADS, 1)
     k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, int heads, int tokens, void* out, __half* out_q8d,
-                   int* err) {
+                   const __grid_constant__ CUtensorMap tmV, int heads, int tokens, int items, void* out,
+                   __half* out_q8d, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;  // tile A, then tile B
-  uint8_t* sK = smem + 2 * TILE_BYTES;
+  uint8_t* sQ = smem;  // [item parity][tile]
+  uint8_t* sK = smem + 4 * TILE_BYTES;
   uint8_t* sV = sK + AST * TILE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + AST * TILE_BYTES);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = q_full + 1;
-  uint64_t* kv_empty = kv_full + AST;
-  uint64_t* s_full = kv_empty + AST;  // [2]
-  uint64_t* p_full = s_full + 2;      // [2]
-  uint64_t* o_full = p_full + 2;      // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
+  uint64_t* q_full = bars;             // [2] per Q buffer
+  uint64_t* q_empty = q_full + 2;      // [2]
+  uint64_t* kv_full = q_empty + 2;     // [AST]
+  uint64_t* kv_empty = kv_full + AST;  // [AST]
+  uint64_t* s_full = kv_empty + AST;   // [2] per tile: S_t(j) ready (and O_t(j-1) done)
+  uint64_t* p_full = s_full + 2;       // [2] per tile
+  uint64_t* o_done = p_full + 2;       // [2] per tile: the item's last O_t finished
+  uint64_t* o_free = o_done + 2;       // [2 tiles][2 buffers]: the item's O has been read
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
-  const int q0 = blockIdx.x * 2 * AQ;
-  const int ntiles = (tokens - q0 > AQ) ? 2 : 1;  // tile B may not exist
+  const int pairs = (tokens + 2 * AQ - 1) / (2 * AQ);  // query-tile pairs per (image, head)
   const int nb = (tokens + AKV - 1) / AKV;
+  auto item_tiles = [&](int it, int& bh, int& q0) {
+    bh = it / pairs;
+    q0 = (it - bh * pairs) * 2 * AQ;
+    return (tokens - q0 > AQ) ? 2 : 1;  // tile 1 may not exist
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&q_full[b], 1);
+      mbar_init(&q_empty[b], 1);
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&o_done[b], 1);
+    }
+    for (int b = 0; b < 4; ++b) mbar_init(&o_free[b], 128);
     for (int s = 0; s < AST; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 128);
-      mbar_init(&o_full[t], 1);
     }
     fence_mbar_init();
   }
@@ -94,58 +105,85 @@ __global__ void __launch_bounds__(A_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, ntiles * TILE_BYTES);
-      for (int t = 0; t < ntiles; ++t) tma_load_3d(sQ + t * TILE_BYTES, &tmQ, q_full, 0, q0 + t * AQ, bh);
-      for (int j = 0; j < nb; ++j) {
-        const int st = j % AST;
-        if (!mbar_wait(&kv_empty[st], ((j / AST) & 1) ^ 1, err, VK_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
-        tma_load_3d(sK + st * TILE_BYTES, &tmK, &kv_full[st], 0, j * AKV, bh);
-        tma_load_3d(sV + st * TILE_BYTES, &tmV, &kv_full[st], 0, j * AKV, bh);
+      uint32_t g = 0;  // K/V blocks loaded so far
+      bool ok = true;
+      for (int it = blockIdx.x, c = 0; it < items && ok; it += gridDim.x, ++c) {
+        int bh, q0;
+        const int ntiles = item_tiles(it, bh, q0);
+        const int qb = c & 1;
+        if (c >= 2 && !mbar_wait(&q_empty[qb], ((c >> 1) - 1) & 1, err, VK_DEV_TIMEOUT_PRODUCER)) break;
+        mbar_arrive_expect_tx(&q_full[qb], ntiles * TILE_BYTES);
+        for (int t = 0; t < ntiles; ++t)
+          tma_load_3d(sQ + (qb * 2 + t) * TILE_BYTES, &tmQ, &q_full[qb], 0, q0 + t * AQ, bh);
+        for (int j = 0; j < nb; ++j, ++g) {
+          const uint32_t st = g % AST;
+          if (!mbar_wait(&kv_empty[st], ((g / AST) & 1) ^ 1, err, VK_DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+          tma_load_3d(sK + st * TILE_BYTES, &tmK, &kv_full[st], 0, j * AKV, bh);
+          tma_load_3d(sV + st * TILE_BYTES, &tmV, &kv_full[st], 0, j * AKV, bh);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(128, 128);
       constexpr uint32_t idO = idesc_bf16_bmn(128, 64);
-      // S_t(j) into tile t's S / P columns; the tensor core runs MMAs in
-      // issue order, so it overwrites P_t(j-1) only after O_t(j-1) read it
-      auto issue_s = [&](int t, int j) {
-        const uint64_t qdesc = smem_desc_k_sw128(smem_u32(sQ + t * TILE_BYTES));
-        const uint64_t kdesc = smem_desc_k_sw128(smem_u32(sK + (j % AST) * TILE_BYTES));
+      auto issue_s = [&](int t, int qb, uint32_t st) {
+        const uint64_t qdesc = smem_desc_k_sw128(smem_u32(sQ + (qb * 2 + t) * TILE_BYTES));
+        const uint64_t kdesc = smem_desc_k_sw128(smem_u32(sK + st * TILE_BYTES));
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_f16(tmem + t * TILE_COLS + COL_S, qdesc + static_cast<uint64_t>(k * 2),
                    kdesc + static_cast<uint64_t>(k * 2), idS, k > 0 ? 1u : 0u);
       };
-      bool ok = mbar_wait(q_full, 0, err, VK_DEV_TIMEOUT_MMA) && mbar_wait(&kv_full[0], 0, err, VK_DEV_TIMEOUT_MMA);
-      if (ok) {
+      uint32_t g = 0;                 // K/V blocks consumed so far
+      uint32_t sp[2] = {0u, 0u};      // per tile: S / P hand-offs so far
+      uint32_t ct[2] = {0u, 0u};      // per tile: items so far
+      bool ok = true;
+      for (int it = blockIdx.x, c = 0; it < items && ok; it += gridDim.x, ++c) {
+        int bh, q0;
+        const int ntiles = item_tiles(it, bh, q0);
+        const int qb = c & 1;
+        if (!(ok = mbar_wait(&q_full[qb], (c >> 1) & 1, err, VK_DEV_TIMEOUT_MMA))) break;
+        if (!(ok = mbar_wait(&kv_full[g % AST], (g / AST) & 1, err, VK_DEV_TIMEOUT_MMA))) break;
         tc_fence_after();
-        for (int t = 0; t < ntiles; ++t) {
-          issue_s(t, 0);
+        for (int t = 0; t < ntiles; ++t) {  // the previous item's last O_t was issued before
+          issue_s(t, qb, g % AST);
           umma_commit(&s_full[t]);
         }
-      }
-      for (int j = 0; j < nb && ok; ++j) {
-        const bool more = j + 1 < nb;
-        if (more && !(ok = mbar_wait(&kv_full[(j + 1) % AST], ((j + 1) / AST) & 1, err, VK_DEV_TIMEOUT_MMA))) break;
-        const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(sV + (j % AST) * TILE_BYTES));
-        for (int t = 0; t < ntiles && ok; ++t) {
-          if (!(ok = mbar_wait(&p_full[t], j & 1, err, VK_DEV_TIMEOUT_MMA))) break;
-          tc_fence_after();
-          const uint32_t base = tmem + t * TILE_COLS;
+        for (int j = 0; j < nb && ok; ++j, ++g) {
+          const bool more = j + 1 < nb;
+          if (more && !(ok = mbar_wait(&kv_full[(g + 1) % AST], ((g + 1) / AST) & 1, err, VK_DEV_TIMEOUT_MMA))) break;
+          const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(sV + (g % AST) * TILE_BYTES));
+          for (int t = 0; t < ntiles && ok; ++t) {
+            if (!(ok = mbar_wait(&p_full[t], sp[t] & 1, err, VK_DEV_TIMEOUT_MMA))) break;
+            ++sp[t];
+            const uint32_t ob = ct[t] & 1;
+            // the first O of an item overwrites buffer ob: item ct-2's output must have been read
+            if (j == 0 && ct[t] >= 2 &&
+                !(ok = mbar_wait(&o_free[t * 2 + ob], ((ct[t] >> 1) - 1) & 1, err, VK_DEV_TIMEOUT_MMA)))
+              break;
+            tc_fence_after();
+            const uint32_t base = tmem + t * TILE_COLS;
 #pragma unroll
-          for (int k = 0; k < AKV / 16; ++k)
-            umma_f16_ts(base + COL_O, base + COL_S + static_cast<uint32_t>(k * 8),
-                        vdesc + static_cast<uint64_t>(k * (2048 >> 4)), idO, (j | k) > 0 ? 1u : 0u);
-          if (more) {
-            issue_s(t, j + 1);
-            umma_commit(&s_full[t]);  // also covers O_t(j)
-          } else {
-            umma_commit(&o_full[t]);
+            for (int k = 0; k < AKV / 16; ++k)
+              umma_f16_ts(base + COL_O + ob * 64, base + COL_S + static_cast<uint32_t>(k * 8),
+                          vdesc + static_cast<uint64_t>(k * (2048 >> 4)), idO, (j | k) > 0 ? 1u : 0u);
+            if (more) {
+              issue_s(t, qb, (g + 1) % AST);
+              umma_commit(&s_full[t]);  // also covers O_t(j)
+            } else {
+              umma_commit(&o_done[t]);
+            }
           }
+          if (ok) umma_commit(&kv_empty[g % AST]);  // after every MMA that read this stage
         }
-        if (ok) umma_commit(&kv_empty[j % AST]);  // after every MMA that read stage j
+        if (!ok) break;
+        umma_commit(&q_empty[qb]);  // every S of this item has been issued
+        for (int t = 0; t < ntiles; ++t) ++ct[t];
       }
     }
   } else {
@@ -153,109 +191,117 @@ __global__ void __launch_bounds__(A_THREADS, 1)
     const int quad = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t tb = tmem + t * TILE_COLS + lane_base;
-    const int qrow = q0 + t * AQ + quad * 32 + lane;
     const float sl2 = 0.125f * 1.4426950408889634f;  // (1/sqrt(64)) * log2(e)
-    float m_ref = -INFINITY;
-    float l_run = 0.0f;
-    bool ok = t < ntiles;
-    for (int j = 0; j < nb && ok; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+    uint32_t sp = 0, ct = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+      int bh, q0;
+      if (t >= item_tiles(it, bh, q0)) continue;
+      const int qrow = q0 + t * AQ + quad * 32 + lane;
+      const uint32_t col_o = COL_O + (ct & 1) * 64;
+      float m_ref = -INFINITY;
+      float l_run = 0.0f;
+      for (int j = 0; j < nb; ++j, ++sp) {
+        if (!mbar_wait(&s_full[t], sp & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int valid = tokens - j * AKV;
+        const bool full_block = valid >= AKV;
+        // block max over S(j), 32 TMEM columns at a time
+        auto block_max = [&]() -> float {
+          float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tb + COL_S + c * 32, r);
+            tmem_wait_ld();
+            if (full_block) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 2)
+                pm[(i >> 1) & 3] = max3f(pm[(i >> 1) & 3], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (c * 32 + i < valid) pm[i & 3] = fmaxf(pm[i & 3], __uint_as_float(r[i]));
+            }
+          }
+          return fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])) * sl2;
+        };
+        // p = 2^(s * log2e / 8 - m) packed as bf16 pairs into pk; returns the row sum
+        uint32_t pk[64];
+        auto exp_pass = [&](float m) -> float {
+          float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+          const float2 scale2 = make_float2(sl2, sl2), shift2 = make_float2(-m, -m);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tb + COL_S + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int k0 = c * 32 + 2 * i;
+              const float2 x = ffma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), scale2, shift2);
+              float2 pp = ((POLY_MASK >> i) & 1) ? exp2_poly2(x)                                  // FMA pipe
+                                                 : make_float2(ex2_approx(x.x), ex2_approx(x.y));  // MUFU
+              if (!full_block) {
+                pp.x = k0 < valid ? pp.x : 0.0f;
+                pp.y = k0 + 1 < valid ? pp.y : 0.0f;
+              }
+              ps[i & 1] = fadd2(ps[i & 1], pp);
+              pk[c * 16 + i] = pack_bf16x2(pp.x, pp.y);
+            }
+          }
+          return (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y);
+        };
+        if (j == 0) m_ref = block_max();
+        // One pass against the running reference m_ref (the max of block 0, or
+        // of a later block that outgrew it).  Probabilities above 1 are fine:
+        // the final O / l is invariant to the reference, and f32 / bf16 hold
+        // p up to 2^127.  Only when a row's block sum passes 2^64 is the block
+        // redone against its own max, with O and l rescaled to match (O_t(j-1)
+        // is complete: S_t(j) was issued after it).
+        float l_blk = exp_pass(m_ref);
+        if (j > 0 && __any_sync(0xffffffffu, !(l_blk < 18446744073709551616.0f))) {  // TMEM access is warp-collective
+          const float m_new = fmaxf(m_ref, block_max());
+          const float f = ex2_approx(m_ref - m_new);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t o[32];
+            tmem_ld32(tb + col_o + h * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * f);
+            tmem_st32(tb + col_o + h * 32, o);
+          }
+          l_run *= f;
+          m_ref = m_new;
+          l_blk = exp_pass(m_ref);
+        }
+        // P over the first 64 columns of S (S is no longer needed)
+        tmem_st32(tb + COL_S, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+        tmem_st32(tb + COL_S + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[t]);
+        l_run += l_blk;
+      }
+      if (!ok || !mbar_wait(&o_done[t], ct & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int valid = tokens - j * AKV;
-      const bool full_block = valid >= AKV;
-      // block max over S(j), 32 TMEM columns at a time
-      auto block_max = [&]() -> float {
-        float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tb + COL_S + c * 32, r);
-          tmem_wait_ld();
-          if (full_block) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 2)
-              pm[(i >> 1) & 3] = max3f(pm[(i >> 1) & 3], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c * 32 + i < valid) pm[i & 3] = fmaxf(pm[i & 3], __uint_as_float(r[i]));
-          }
-        }
-        return fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])) * sl2;
-      };
-      // p = 2^(s * log2e / 8 - m) packed as bf16 pairs into pk; returns the row sum
-      uint32_t pk[64];
-      auto exp_pass = [&](float m) -> float {
-        float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-        const float2 scale2 = make_float2(sl2, sl2), shift2 = make_float2(-m, -m);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tb + COL_S + c * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int k0 = c * 32 + 2 * i;
-            const float2 x = ffma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), scale2, shift2);
-            float2 pp = ((POLY_MASK >> i) & 1) ? exp2_poly2(x)                                  // FMA pipe
-                                               : make_float2(ex2_approx(x.x), ex2_approx(x.y));  // MUFU
-            if (!full_block) {
-              pp.x = k0 < valid ? pp.x : 0.0f;
-              pp.y = k0 + 1 < valid ? pp.y : 0.0f;
-            }
-            ps[i & 1] = fadd2(ps[i & 1], pp);
-            pk[c * 16 + i] = pack_bf16x2(pp.x, pp.y);
-          }
-        }
-        return (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y);
-      };
-      if (j == 0) m_ref = block_max();
-      // One pass against the running reference m_ref (the max of block 0, or
-      // of a later block that outgrew it).  Probabilities above 1 are fine:
-      // the final O / l is invariant to the reference, and f32 / bf16 hold
-      // p up to 2^127.  Only when a row's block sum passes 2^64 is the block
-      // redone against its own max, with O and l rescaled to match (O_t(j-1)
-      // is complete: S_t(j) was issued after it).
-      float l_blk = exp_pass(m_ref);
-      if (j > 0 && __any_sync(0xffffffffu, !(l_blk < 18446744073709551616.0f))) {  // TMEM access is warp-collective
-        const float m_new = fmaxf(m_ref, block_max());
-        const float f = ex2_approx(m_ref - m_new);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t o[32];
-          tmem_ld32(tb + COL_O + h * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * f);
-          tmem_st32(tb + COL_O + h * 32, o);
-        }
-        l_run *= f;
-        m_ref = m_new;
-        l_blk = exp_pass(m_ref);
-      }
-      // P over the first 64 columns of S (S is no longer needed)
-      tmem_st32(tb + COL_S, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-      tmem_st32(tb + COL_S + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[t]);
-      l_run += l_blk;
-    }
-    if (ok && mbar_wait(&o_full[t], 0, err, VK_DEV_TIMEOUT_EPILOGUE)) {
-      tc_fence_after();
       float o[64];
       const float inv = 1.0f / l_run;
+      tmem_ld32(tb + col_o, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+      tmem_ld32(tb + col_o + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&o_free[t * 2 + (ct & 1)]);  // O is in registers: item ct+2 may overwrite it
+      ++ct;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t r0[32];
-        tmem_ld32(tb + COL_O + h * 32, r0);
-        tmem_wait_ld();
-#pragma unroll
-        for (int d = 0; d < 32; ++d) o[h * 32 + d] = __uint_as_float(r0[d]) * inv;
-      }
+      for (int d = 0; d < 64; ++d) o[d] *= inv;
       if (qrow < tokens) {
         const int b_img = bh / heads, h = bh - b_img * heads;
         if constexpr (OUT == ATTN_OUT_HEAD_F32) {
@@ -317,8 +363,9 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  dim3 grid((tokens + 2 * AQ - 1) / (2 * AQ), images * heads);
-  k_attention_tc<OUT><<<grid, A_THREADS, ATT_SMEM, s>>>(mq, mk, mv, heads, tokens, out, q8d, err);
+  const int items = ((tokens + 2 * AQ - 1) / (2 * AQ)) * images * heads;
+  const int grid = items < num_sms() ? items : num_sms();
+  k_attention_tc<OUT><<<grid, A_THREADS, ATT_SMEM, s>>>(mq, mk, mv, heads, tokens, items, out, q8d, err);
   return cudaGetLastError();
 }
 
