@@ -8,14 +8,16 @@
 //
 // One tcgen05.mma.kind::i8 with K = 32 is exactly one Q8_0 block, so every
 // block's int32 dot products land in their own TMEM accumulator (4 rotating
-// buffers of 128 columns).  Eight epilogue warps drain each buffer with
+// buffers of 128 columns).  Sixteen epilogue warps drain each buffer with
 // tcgen05.ld and fold it into f32 registers in the reference's order:
-// acc = acc + (d_a * d_b) * float(isum), rounded at every step (no FMA), so
-// the f32 result equals the reference scalar oracle bit for bit.
+// acc = acc + (d_a * d_b) * float(isum).  The f32-output operator
+// (vk_gemm_q8_0) rounds at every step (no FMA), so its result equals the
+// reference scalar oracle bit for bit; the encoder's fused epilogues fold
+// with one FMA per step (the int32 block dots are exact either way).
 //
 //   warp 0       TMA producer: A / W int8 tiles [128 x 128 bytes], 128B swizzle
 //   warp 1       TMEM owner; one lane issues one MMA per Q8_0 block
-//   warps 2..9   epilogue: two warps per TMEM lane quadrant, 64 columns each
+//   warps 2..17  epilogue: four warps per TMEM lane quadrant, 32 columns each
 #include "vk_common.cuh"
 #include "vk_epilogue.cuh"
 #include "vk_internal.h"
@@ -28,8 +30,8 @@ constexpr int QBN = 128;
 constexpr int QBK = 128;  // bytes = int8 elements = 4 Q8_0 blocks per stage
 constexpr int QSTAGES = 4;
 constexpr int QNACC = 4;  // TMEM accumulators of QBN columns
-constexpr int Q_THREADS = 320;
-constexpr int Q_EPI_THREADS = 256;
+constexpr int Q_THREADS = 576;  // producer, MMA, 16 epilogue warps
+constexpr int Q_EPI_THREADS = 512;
 constexpr int Q_A_BYTES = QBM * QBK;
 constexpr int Q_B_BYTES = QBN * QBK;
 constexpr int Q_STAGE_BYTES = Q_A_BYTES + Q_B_BYTES;
@@ -147,9 +149,9 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
       }
     }
   } else {
-    const int et = threadIdx.x - 64;  // 0..255
+    const int et = threadIdx.x - 64;  // 0..511
     const int quad = warp & 3;
-    const int chalf = (warp - 2) >> 2;  // columns [64 * chalf, 64 * chalf + 64)
+    const int cq = (warp - 2) >> 2;  // columns [32 * cq, 32 * cq + 32) of the tile
     uint32_t blk = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
@@ -162,12 +164,15 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
         sWd[i] = __half2float(Wd[static_cast<size_t>(n0 + c) * nb + b]);
       }
       epi_bar();
-      float acc[64];
+      float acc[32];
 #pragma unroll
-      for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+      for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
       const __half* arow = Ad + static_cast<size_t>(row < M ? row : 0) * nb;
+      float da_next = __half2float(__ldg(arow));  // activation scales run one block ahead
 #pragma unroll 1
       for (int b = 0; b < nb; ++b, ++blk) {
+        const float da = da_next;
+        if (b + 1 < nb) da_next = __half2float(__ldg(arow + b + 1));
         const uint32_t buf = blk % QNACC;
         const uint32_t bph = (blk / QNACC) & 1u;
         if (!mbar_wait(&tfull[buf], bph, err, VK_DEV_TIMEOUT_EPILOGUE)) {
@@ -175,40 +180,54 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
           break;
         }
         tc_fence_after();
-        uint32_t r0[32], r1[32];
-        const uint32_t ta = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * QBN + chalf * 64;
+        uint32_t r0[32];
+        const uint32_t ta = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * QBN + cq * 32;
         tmem_ld32(ta, r0);
-        tmem_ld32(ta + 32, r1);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&tempty[buf]);
-        const float da = __half2float(__ldg(arow + b));
-        const float4* wd4 = reinterpret_cast<const float4*>(sWd + b * QBN + chalf * 64);
+        const float4* wd4 = reinterpret_cast<const float4*>(sWd + b * QBN + cq * 32);
+        // acc + (d_a * d_b) * isum, each step rounded (src/scalar.rs:47-52),
+        // the multiplies two columns per packed f32x2 operation (IEEE
+        // round-to-nearest per lane, as the scalar steps).  |isum| <= 32 * 127^2 < 2^22, so
+        // float(isum) is exact and comes from the bits of 1.5 * 2^23 + isum
+        // minus 1.5 * 2^23 on the integer and FMA pipes.
+        const float2 da2 = make_float2(da, da);
+        const float2 magic2 = make_float2(12582912.0f, 12582912.0f);
 #pragma unroll
-        for (int j4 = 0; j4 < 16; ++j4) {
+        for (int j4 = 0; j4 < 8; ++j4) {
           const float4 db = wd4[j4];
-          const float dbv[4] = {db.x, db.y, db.z, db.w};
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int j = j4 * 4 + t;
-            const int32_t is = static_cast<int32_t>(j < 32 ? r0[j] : r1[j - 32]);
-            acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(da, dbv[t]), __int2float_rn(is)));
-            if constexpr (DUMP) {
-              if (row < M) dots[(static_cast<size_t>(row) * N + n0 + chalf * 64 + j) * nb + b] = is;
+          for (int h = 0; h < 2; ++h) {
+            const int j = j4 * 4 + 2 * h;
+            const float2 s2 = fmul2(da2, h == 0 ? make_float2(db.x, db.y) : make_float2(db.z, db.w));
+            const float2 f2 = fsub2(make_float2(__int_as_float(static_cast<int32_t>(r0[j]) + 0x4B400000),
+                                                __int_as_float(static_cast<int32_t>(r0[j + 1]) + 0x4B400000)),
+                                    magic2);
+            if constexpr (MODE == EPI_F32) {
+              // the adds stay scalar: a packed multiply feeding a packed add
+              // was contracted into a fused multiply-add, which rounds once
+              const float2 p2 = fmul2(s2, f2);
+              acc[j] = __fadd_rn(acc[j], p2.x);
+              acc[j + 1] = __fadd_rn(acc[j + 1], p2.y);
+            } else {
+              // encoder epilogues: one fused multiply-add per column (the
+              // block dots stay exact; the sum is within tolerance)
+              const float2 a2 = ffma2(s2, f2, make_float2(acc[j], acc[j + 1]));
+              acc[j] = a2.x;
+              acc[j + 1] = a2.y;
             }
+          }
+          if constexpr (DUMP) {
+            if (row < M)
+              for (int t = 0; t < 4; ++t)
+                dots[(static_cast<size_t>(row) * N + n0 + cq * 32 + j4 * 4 + t) * nb + b] =
+                    static_cast<int32_t>(r0[j4 * 4 + t]);
           }
         }
       }
       if (!ok) break;
-      if (row < M) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = acc[c * 32 + j];
-          epilogue_chunk<MODE>(epi, row, n0 + chalf * 64 + c * 32, N, v);
-        }
-      }
+      if (row < M) epilogue_chunk<MODE>(epi, row, n0 + cq * 32, N, acc);
     }
   }
   __syncthreads();
