@@ -235,15 +235,16 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
           const float2 scale2 = make_float2(sl2, sl2), shift2 = make_float2(-m, -m);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tb + COL_S + c * 32, r);
+          for (int c = 0; c < 4; c += 2) {
+            uint32_t rr[64];
+            tmem_ld32(tb + COL_S + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+            tmem_ld32(tb + COL_S + c * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
+            for (int i = 0; i < 32; ++i) {
               const int k0 = c * 32 + 2 * i;
-              const float2 x = ffma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), scale2, shift2);
-              float2 pp = ((POLY_MASK >> i) & 1) ? exp2_poly2(x)                                  // FMA pipe
+              const float2 x = ffma2(make_float2(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), scale2, shift2);
+              float2 pp = ((POLY_MASK >> (i & 15)) & 1) ? exp2_poly2(x)                                  // FMA pipe
                                                  : make_float2(ex2_approx(x.x), ex2_approx(x.y));  // MUFU
               if (!full_block) {
                 pp.x = k0 < valid ? pp.x : 0.0f;
