@@ -112,14 +112,16 @@ int ensure_rope(vk_encoder* enc, size_t gh, size_t gw) {
     enc->seen.clear();
   }
   // Two layouts of the same values: [t][axis][i](sin, cos) for the f32 RoPE
-  // pass, and [axis * 16 + i][t](sin, cos) for the GEMM epilogue, where the
-  // 32 threads of a warp hold 32 consecutive tokens (coalesced reads).
+  // pass, and [axis * 8 + i / 2][t](sin_i, cos_i, sin_i+1, cos_i+1) for the
+  // GEMM epilogue, where the 32 threads of a warp hold 32 consecutive tokens
+  // (coalesced 16-byte reads, two frequencies each).
   std::vector<float> both(2 * rot.size());
   std::copy(rot.begin(), rot.end(), both.begin());
   for (size_t t = 0; t < T; ++t)
     for (size_t ai = 0; ai < 32; ++ai) {
-      both[rot.size() + (ai * T + t) * 2] = rot[(t * 32 + ai) * 2];
-      both[rot.size() + (ai * T + t) * 2 + 1] = rot[(t * 32 + ai) * 2 + 1];
+      const size_t dst = rot.size() + ((ai / 2) * T + t) * 4 + (ai & 1) * 2;
+      both[dst] = rot[(t * 32 + ai) * 2];
+      both[dst + 1] = rot[(t * 32 + ai) * 2 + 1];
     }
   VK_TRY_CUDA(cudaMalloc(&enc->rope, both.size() * sizeof(float)), "rotation table");
   VK_TRY_CUDA(cudaMemcpy(enc->rope, both.data(), both.size() * sizeof(float), cudaMemcpyHostToDevice), "rotation table");

@@ -61,13 +61,16 @@ __device__ __forceinline__ void epi_math(const GemmEpi& p, int row, int col0, fl
     if (p.rope != nullptr && q.g < 2) {
       // Axial RoPE, rotate-half pairing (i, i + 16) inside this 32-wide axis
       // half (src/rope.rs:84-93); the chunk is exactly one axis half.
-      const float2* r = reinterpret_cast<const float2*>(p.rope) + static_cast<size_t>(q.axis * 16) * p.tokens + q.t;
+      const float4* r = reinterpret_cast<const float4*>(p.rope) + static_cast<size_t>(q.axis * 8) * p.tokens + q.t;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float2 sc = __ldg(r + static_cast<size_t>(i) * p.tokens);  // (sin, cos)
-        const float a = v[i], b = v[i + 16];
-        v[i] = a * sc.y - b * sc.x;
-        v[i + 16] = b * sc.y + a * sc.x;
+      for (int i2 = 0; i2 < 8; ++i2) {
+        const float4 sc = __ldg(r + static_cast<size_t>(i2) * p.tokens);  // (sin, cos) of 2 i2, 2 i2 + 1
+        const int i = 2 * i2;
+        const float a0 = v[i], b0 = v[i + 16], a1 = v[i + 1], b1 = v[i + 17];
+        v[i] = a0 * sc.y - b0 * sc.x;
+        v[i + 16] = b0 * sc.y + a0 * sc.x;
+        v[i + 1] = a1 * sc.w - b1 * sc.z;
+        v[i + 17] = b1 * sc.w + a1 * sc.z;
       }
     }
   }

@@ -33,7 +33,7 @@ struct GemmEpi {
   void* q = nullptr;             // [images, heads, tokens, 64]
   void* k = nullptr;
   void* v = nullptr;
-  const float* rope = nullptr;   // [2 * 16, tokens] of (sin, cos): [axis * 16 + i][t], or null
+  const float* rope = nullptr;   // [2 * 8, tokens] of (sin_i, cos_i, sin_i+1, cos_i+1): [axis * 8 + i / 2][t], or null
   int tokens = 0;                // rows per image
   int heads = 0;                 // embed = heads * 64
   int8_t* q8 = nullptr;          // [M, N] int8 quants (EPI_Q8_GELU)
