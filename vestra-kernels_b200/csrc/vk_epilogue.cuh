@@ -55,7 +55,16 @@ __device__ __forceinline__ void epi_math(const GemmEpi& p, int row, int col0, fl
     }
   } else if constexpr (MODE == EPI_BF16_GELU || MODE == EPI_Q8_GELU) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = FAST_GELU ? gelu_erf_fast(v[j]) : gelu_erf(v[j]);
+    for (int j = 0; j < 32; j += 2) {
+      if constexpr (FAST_GELU) {
+        const float2 g = gelu_erf_ex2(make_float2(v[j], v[j + 1]));
+        v[j] = g.x;
+        v[j + 1] = g.y;
+      } else {
+        v[j] = gelu_erf(v[j]);
+        v[j + 1] = gelu_erf(v[j + 1]);
+      }
+    }
   } else if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32) {
     const QkvPos q = qkv_pos(p, row, col0);
     if (p.rope != nullptr && q.g < 2) {
