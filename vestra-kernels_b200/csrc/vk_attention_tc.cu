@@ -41,8 +41,10 @@ constexpr int A_THREADS = 320; // producer, MMA, 2 x 4 softmax warps
 constexpr int TILE_BYTES = 128 * 128;  // 128 rows x 64 bf16
 // Pairs i (of the 16 per 32-column chunk) whose exponentials use the
 // FMA-pipe polynomial instead of MUFU ex2 (16 lanes per clock per SM).
+// Measured on the current kernel: 0 (all MUFU) is fastest; 4, 6 and 8 of
+// 16 on the polynomial cost 1-4 %.
 #ifndef VK_ATT_POLY_MASK
-#define VK_ATT_POLY_MASK 0x2929u
+#define VK_ATT_POLY_MASK 0x0u
 #endif
 constexpr uint32_t POLY_MASK = VK_ATT_POLY_MASK;
 constexpr uint32_t COL_S = 0, COL_O = 128, TILE_COLS = 256;  // S / P [0, 128), O buffers [128, 192), [192, 256)
