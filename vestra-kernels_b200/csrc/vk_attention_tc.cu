@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dependency_wait();  // q, k, v from the QKV GEMM are visible from here
 
   if (warp == 0) {
     if (lane == 0) {
@@ -368,8 +369,17 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
   }
   const int items = ((tokens + 2 * AQ - 1) / (2 * AQ)) * images * heads;
   const int grid = items < num_sms() ? items : num_sms();
-  k_attention_tc<OUT><<<grid, A_THREADS, ATT_SMEM, s>>>(mq, mk, mv, heads, tokens, items, out, q8d, err);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(A_THREADS);
+  cfg.dynamicSmemBytes = ATT_SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute la[1];
+  la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  la[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = la;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_attention_tc<OUT>, mq, mk, mv, heads, tokens, items, out, q8d, err);
 }
 
 cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int images,

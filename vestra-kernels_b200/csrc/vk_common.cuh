@@ -47,6 +47,14 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
                : "memory");
 }
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute is scheduled as the previous kernel's CTAs
+// exit, not after the whole grid.  It sets up (barriers, TMEM, descriptor
+// prefetch), then waits here until the previous grid has completed and its
+// writes are visible, before touching global memory.  (No kernel triggers
+// its dependents early: measured, that made the chain slower.)  Without the
+// attribute the wait returns at once.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

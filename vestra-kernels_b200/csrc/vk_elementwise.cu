@@ -40,6 +40,7 @@ template <int VPL>  // float4 vectors per lane; cols == VPL * 128
 __global__ void __launch_bounds__(EW_THREADS)
     k_layernorm_vec(const float* __restrict__ x, float* y, __nv_bfloat16* yb, int8_t* yq, __half* yd,
                     int rows, int cols, const float* __restrict__ g, const float* __restrict__ b, float eps) {
+  grid_dependency_wait();  // x from the previous kernel is visible from here
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -124,9 +125,18 @@ cudaError_t layernorm_f32(const float* x, float* y, __nv_bfloat16* yb, int8_t* y
     k_layernorm_generic<<<grid, EW_THREADS, 0, s>>>(x, y, rows, cols, g, b, eps);
     return cudaGetLastError();
   }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(EW_THREADS);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   switch (cols / 128) {
 #define VK_LN_CASE(n) \
-  case n: k_layernorm_vec<n><<<grid, EW_THREADS, 0, s>>>(x, y, yb, yq, yd, rows, cols, g, b, eps); break;
+  case n: return cudaLaunchKernelEx(&cfg, k_layernorm_vec<n>, x, y, yb, yq, yd, rows, cols, g, b, eps);
     VK_LN_CASE(1) VK_LN_CASE(2) VK_LN_CASE(3) VK_LN_CASE(4) VK_LN_CASE(5) VK_LN_CASE(6) VK_LN_CASE(7)
     VK_LN_CASE(8)
 #undef VK_LN_CASE

@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  grid_dependency_wait();  // the previous kernel's outputs are visible from here
 
   if (warp == 0) {
     if (lane == 0) {
@@ -246,8 +247,17 @@ static cudaError_t launch_q8(const CUtensorMap& ta, const CUtensorMap& tb, const
   if (e != cudaSuccess) return e;
   const int tiles = ((M + QBM - 1) / QBM) * (N / QBN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  k_gemm_q8<MODE, DUMP><<<grid, Q_THREADS, smem, s>>>(ta, tb, Ad, Wd, epi, M, N, K, dots, err);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Q_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_gemm_q8<MODE, DUMP>, ta, tb, Ad, Wd, epi, M, N, K, dots, err);
 }
 
 cudaError_t gemm_q8_tc(const int8_t* Aq, const __half* Ad, const int8_t* Wq, const __half* Wd, int M, int N, int K,

@@ -50,6 +50,8 @@ bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
                   uint32_t box1, CUtensorMapSwizzle swz);
 
 int num_sms();
+// Launch attributes for programmatic dependent launch (off with VK_NO_PDL).
+bool pdl_enabled();
 
 // bf16 x bf16 -> f32 tcgen05 GEMM: C[M,N] = A[M,K] . W[N,K]^T (both K-major),
 // K % 64 == 0, N % 128 == 0.  Returns a cudaError_t.

@@ -1,3 +1,4 @@
+#include <stdlib.h>
 // vk_tmap.cu -- host helpers shared by the TMA kernels: tensor-map encoding
 // (driver entry point fetched through the runtime, no libcuda link) and the
 // SM count.
@@ -48,6 +49,11 @@ bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
   CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+bool pdl_enabled() {
+  static const bool on = getenv("VK_NO_PDL") == nullptr;
+  return on;
 }
 
 int num_sms() {
