@@ -145,6 +145,36 @@ int vk_gemm_q8_0_block_dots(vk_ctx* ctx, size_t m, size_t n, size_t k,
 int vk_gemm_q8_0_noalloc(void* stream, size_t m, size_t n, size_t k, const vk_block_q8_0* a_q,
                          const vk_block_q8_0* b_q, float* c);
 
+/* ------------------------------------------------- patch embedding
+ * The step before the encoder.  src/cuda.rs:295-316 vestra_patchify_nchw_f32
+ * / CudaRuntime::patchify_nchw_f32 (src/cuda.rs:1073): image [channels,
+ * height, width] (device) -> patches [(height/patch) * (width/patch),
+ * channels * patch * patch], each row in (channel, patch_y, patch_x) order.
+ * Invalid shapes (zero sizes, height or width not a multiple of patch) are
+ * VK_ERR_INVALID_ARGUMENT, as the reference's CudaError::Kernel. */
+int vk_patchify_nchw_f32(vk_ctx* ctx, const float* image, size_t height, size_t width, size_t patch,
+                         size_t channels, float* patches);
+/* src/cuda.rs:321-334 vestra_prepend_cls_add_pos_f32 /
+ * CudaRuntime::prepend_cls_add_pos_f32 (src/cuda.rs:1130): tokens
+ * [patch_count + 1, embed] = [cls; patches] + position (device). */
+int vk_prepend_cls_add_pos_f32(vk_ctx* ctx, const float* patches, const float* cls, const float* position,
+                               size_t patch_count, size_t embed, float* tokens);
+
+/* Batched patch embedding as one call: tokens[b] = [cls; patchify(image[b])
+ * . weight + bias] + position.  weight_host [channels * patch * patch, embed]
+ * (the OIHW convolution weight flattened input-major), bias / cls [embed]
+ * (host); math VK_MATH_F32 (FMA projection, bit-exact with the f32
+ * operators) or VK_MATH_BF16 (tensor cores; embed % 128 == 0). */
+typedef struct vk_patch_embed vk_patch_embed;
+int vk_patch_embed_prepare(vk_ctx* ctx, size_t channels, size_t patch, size_t embed, const float* weight_host,
+                           const float* bias_host, const float* cls_host, int math, vk_patch_embed** out);
+/* images_dev [images, channels, height, width]; position_dev [tokens, embed]
+ * with tokens = (height/patch) * (width/patch) + 1; tokens_dev [images,
+ * tokens, embed] (position and tokens 16-byte aligned). */
+int vk_patch_embed_forward(vk_ctx* ctx, const vk_patch_embed* pe, size_t images, size_t height, size_t width,
+                           const float* images_dev, const float* position_dev, float* tokens_dev);
+int vk_patch_embed_release(vk_patch_embed* pe);
+
 /* --------------------------------------------------------- prepared values
  * Mirrors the prepared-value objects of the reference (CudaLinearF32,
  * src/cuda.rs:1233-1334): weights are converted and laid out once. */

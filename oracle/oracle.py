@@ -246,6 +246,25 @@ def linear_fma(a, b) -> np.ndarray:
     return linear_bias_scale(a, b, np.zeros(np.shape(b)[1], np.float32), np.ones(np.shape(b)[1], np.float32))
 
 
+def patchify_nchw(image, height, width, patch, channels) -> np.ndarray:
+    """vestra_patchify_nchw_f32 (src/cuda.rs:295-316); raises on an invalid shape."""
+    image = _f32(image)
+    rows = (height // patch) * (width // patch) if patch else 0
+    out = np.empty((rows, channels * patch * patch), np.float32)
+    lib().vko_patchify_nchw.restype = ctypes.c_int
+    if lib().vko_patchify_nchw(_p(image), _sz(height), _sz(width), _sz(patch), _sz(channels), _p(out)) != 0:
+        raise ValueError("invalid NCHW patchify shape")
+    return out
+
+
+def prepend_cls_add_pos(patches, cls, position, patch_count, embed) -> np.ndarray:
+    """vestra_prepend_cls_add_pos_f32 (src/cuda.rs:321-334)."""
+    out = np.empty((patch_count + 1, embed), np.float32)
+    lib().vko_prepend_cls_add_pos(_p(_f32(patches)), _p(_f32(cls)), _p(_f32(position)), _sz(patch_count), _sz(embed),
+                                  _p(out))
+    return out
+
+
 class _Layer(ctypes.Structure):
     _fields_ = [(n, _f) for n in (
         "ln1_g", "ln1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ls1",

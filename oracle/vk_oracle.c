@@ -18,6 +18,34 @@
 #include <omp.h>
 #endif
 
+/* src/cuda.rs:295-316 (kernel) and 1073-1093 (shape checks) */
+int vko_patchify_nchw(const float* image, size_t height, size_t width, size_t patch, size_t channels,
+                      float* patches) {
+  if (height == 0 || width == 0 || patch == 0 || channels == 0 || height % patch != 0 || width % patch != 0)
+    return -1;
+  const size_t area = patch * patch, row_width = channels * area, grid_w = width / patch;
+  const size_t count = (height / patch) * grid_w * row_width;
+  for (size_t index = 0; index < count; ++index) {
+    const size_t p = index / row_width, within = index % row_width;
+    const size_t c = within / area, spatial = within % area;
+    const size_t y = (p / grid_w) * patch + spatial / patch;
+    const size_t x = (p % grid_w) * patch + spatial % patch;
+    patches[index] = image[(c * height + y) * width + x];
+  }
+  return 0;
+}
+
+/* src/cuda.rs:321-334: value + position, cls for token 0 */
+void vko_prepend_cls_add_pos(const float* patches, const float* cls, const float* position, size_t patch_count,
+                             size_t embed, float* tokens) {
+  const size_t len = (patch_count + 1) * embed;
+  for (size_t index = 0; index < len; ++index) {
+    const size_t token = index / embed, channel = index % embed;
+    const float value = token == 0 ? cls[channel] : patches[(token - 1) * embed + channel];
+    tokens[index] = value + position[index];
+  }
+}
+
 void vko_set_threads(int n) {
 #ifdef _OPENMP
   if (n > 0) omp_set_num_threads(n);

@@ -114,6 +114,17 @@ void vko_encoder_layer(float* x, size_t tokens, size_t grid_h, size_t grid_w, si
                        size_t heads, size_t ffn, const vko_layer* w, float eps, float rope_freq,
                        int bf16_points);
 
+/* src/cuda.rs:295-316 vestra_patchify_nchw_f32: image [channels, height,
+ * width] -> patches [(height/patch)(width/patch), channels * patch^2], each
+ * row in (channel, patch_y, patch_x) order.  Returns 0, or -1 on an invalid
+ * shape (src/cuda.rs:1081-1093). */
+int vko_patchify_nchw(const float* image, size_t height, size_t width, size_t patch, size_t channels,
+                      float* patches);
+/* src/cuda.rs:321-334 vestra_prepend_cls_add_pos_f32: tokens [patch_count + 1,
+ * embed] = [cls; patches] + position. */
+void vko_prepend_cls_add_pos(const float* patches, const float* cls, const float* position, size_t patch_count,
+                             size_t embed, float* tokens);
+
 /* Threads used by the parallel loops (rows are independent and each keeps
  * the scalar reduction order, so results do not depend on this). */
 void vko_set_threads(int n);

@@ -67,6 +67,26 @@ def test_cuda_module_gemm_and_bias_scale_values(oracle_lib, kat):
     assert c.ravel().tolist() == case["epilogue"]
 
 
+def test_cuda_module_patchify_values(oracle_lib, kat):
+    case = kat["cuda.patchify_nchw"]
+    image = np.arange(48, dtype=np.float32)
+    got = oracle_lib.patchify_nchw(image, case["height"], case["width"], case["patch"], case["channels"])
+    assert got.ravel().tolist() == case["expected"]
+
+
+@pytest.mark.parametrize("h,w,p,c", [(5, 4, 2, 3), (4, 4, 0, 3), (0, 4, 2, 3), (4, 6, 4, 1)])
+def test_patchify_rejects_invalid_shapes(oracle_lib, h, w, p, c):
+    with pytest.raises(ValueError):
+        oracle_lib.patchify_nchw(np.zeros(max(c * h * w, 1), np.float32), h, w, p, c)
+
+
+def test_cuda_module_prepend_cls_add_pos_values(oracle_lib, kat):
+    case = kat["cuda.prepend_cls_add_pos"]
+    got = oracle_lib.prepend_cls_add_pos(case["patches"], case["cls"], case["position"], case["tokens"],
+                                         case["channels"])
+    assert got.ravel().tolist() == case["expected"]
+
+
 # ---- tests/attention_matches_naive.rs -----------------------------------
 
 @pytest.mark.parametrize("heads,n,hd,seed", [(2, 8, 16, 0x12345678), (4, 37, 32, 0xDEADBEEF), (1, 130, 8, 0x0BADF00D)])

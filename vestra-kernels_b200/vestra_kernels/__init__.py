@@ -76,6 +76,11 @@ SIGNATURES = {
     "vk_encoder_profile": (_I, [_P, _P, _S, _S, _S, _P, _P, _P, _I]),
     "vk_encoder_last_launches": (_I, [_P]),
     "vk_encoder_release": (_I, [_P]),
+    "vk_patchify_nchw_f32": (_I, [_P, _P, _S, _S, _S, _S, _P]),
+    "vk_prepend_cls_add_pos_f32": (_I, [_P, _P, _P, _P, _S, _S, _P]),
+    "vk_patch_embed_prepare": (_I, [_P, _S, _S, _S, _P, _P, _P, _I, ctypes.POINTER(_P)]),
+    "vk_patch_embed_forward": (_I, [_P, _P, _S, _S, _S, _P, _P, _P]),
+    "vk_patch_embed_release": (_I, [_P]),
 }
 
 _lib = None
@@ -332,6 +337,55 @@ class Linear:
         try:
             if self.handle:
                 lib().vk_release_linear(self.handle)
+                self.handle = None
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------- patch embedding
+def patchify_nchw_f32(image, height, width, patch, channels, patches, ctx: Context | None = None) -> None:
+    """CudaRuntime::patchify_nchw_f32 (src/cuda.rs:1073): image [C, H, W] ->
+    patches [(H/p)(W/p), C p p]; invalid shapes raise, as the reference's Err."""
+    ctx = ctx or default_context()
+    _check(lib().vk_patchify_nchw_f32(ctx.handle, _ptr(image), height, width, patch, channels, _ptr(patches)))
+
+
+def prepend_cls_add_pos_f32(patches, cls, position, patch_count, embed, tokens, ctx: Context | None = None) -> None:
+    """CudaRuntime::prepend_cls_add_pos_f32 (src/cuda.rs:1130): tokens = [cls; patches] + position."""
+    ctx = ctx or default_context()
+    _check(lib().vk_prepend_cls_add_pos_f32(ctx.handle, _ptr(patches), _ptr(cls), _ptr(position), patch_count, embed,
+                                            _ptr(tokens)))
+
+
+class PatchEmbed:
+    """Batched DA3 patch embedding: tokens[b] = [cls; patchify(image[b]) . W + b] + position."""
+
+    def __init__(self, ctx: Context, weight_kn, bias, cls, channels: int, patch: int, math: int = MATH_BF16):
+        import numpy as np
+
+        w = np.ascontiguousarray(weight_kn, dtype=np.float32)
+        self.k, self.embed = w.shape
+        if self.k != channels * patch * patch:
+            raise ValueError(f"weight has {self.k} rows, expected channels * patch^2 = {channels * patch * patch}")
+        b = np.ascontiguousarray(bias, dtype=np.float32)
+        c = np.ascontiguousarray(cls, dtype=np.float32)
+        h = ctypes.c_void_p()
+        st = _check(lib().vk_patch_embed_prepare(ctx.handle, channels, patch, self.embed,
+                                                 w.ctypes.data_as(ctypes.c_void_p), b.ctypes.data_as(ctypes.c_void_p),
+                                                 c.ctypes.data_as(ctypes.c_void_p), math, ctypes.byref(h)))
+        if st != VK_OK:
+            raise VestraError(st, last_error())
+        self.handle, self.ctx, self.patch, self.channels = h, ctx, patch, channels
+
+    def __call__(self, images, position, tokens, count: int, height: int, width: int) -> bool:
+        """images [count, C, H, W], position [(H/p)(W/p) + 1, E], tokens [count, tokens, E] (CUDA tensors)."""
+        return _check(lib().vk_patch_embed_forward(self.ctx.handle, self.handle, count, height, width, _ptr(images),
+                                                   _ptr(position), _ptr(tokens))) == VK_OK
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib().vk_patch_embed_release(self.handle)
                 self.handle = None
         except Exception:
             pass
