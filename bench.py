@@ -186,6 +186,32 @@ def run_reference(args, rank, world):
 
 
 # ---------------------------------------------------------------- GPU leg
+def patch_embed_ms(vk, ctx, B, gh, gw, steps, math):
+    """CUDA-event ms per call of the batched patch embedding (random-init
+    weights, images ~U(0, 1)), or None for Q8_0 math (f32 / bf16 only)."""
+    import torch
+
+    if math == vk.MATH_Q8_0:
+        return None
+    r = np.random.default_rng(3)
+    h, w, n = 14 * gh, 14 * gw, gh * gw
+    pe = vk.PatchEmbed(ctx, (r.standard_normal((588, E)) * 0.02).astype(np.float32),
+                       (r.standard_normal(E) * 0.01).astype(np.float32),
+                       (r.standard_normal(E) * 0.02).astype(np.float32), channels=3, patch=14, math=math)
+    imgs = torch.rand(B, 3, h, w, device="cuda")
+    pos = torch.randn(n + 1, E, device="cuda") * 0.02
+    toks = torch.empty(B, n + 1, E, device="cuda")
+    for _ in range(3):
+        pe(imgs, pos, toks, B, h, w)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        pe(imgs, pos, toks, B, h, w)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
 def run_vestra(args, rank, world, local_rank):
     import torch
 
@@ -250,6 +276,10 @@ def run_vestra(args, rank, world, local_rank):
     # per-kernel device time (eager forward with events between kernels)
     slots = enc.profile(x, out, B, gh, gw)
 
+    # the step before the encoder: patch embedding of the same batch (images
+    # [B, 3, 14 gh, 14 gw] -> tokens), timed on its own
+    pe_ms = patch_embed_ms(vk, ctx, B, gh, gw, args.steps, math)
+
     ms, e2e_ms = max_over_ranks(ms), max_over_ranks(e2e_ms)
     if rank != 0:
         return
@@ -295,6 +325,10 @@ def run_vestra(args, rank, world, local_rank):
                      "kernel_ms": {"layernorm": slots[0] + slots[4] if math != vk.MATH_F32 else slots[0] + slots[7],
                                    "gemm": gemm_ms, "attention": attn_ms, "eager_total": total_ms_eager}},
         "clocks": clk.summary(),
+        "patch_embed": None if pe_ms is None else {
+            "ms_per_step": round(pe_ms, 4), "images_per_s": B / (pe_ms / 1e3),
+            "tflops": 2.0 * B * gh * gw * 588 * E / (pe_ms / 1e3) / 1e12,
+            "note": "patchify + 588->768 projection + cls/position assembly of the same batch, outside `value`"},
     }
     if world == 1 and not args.no_cpu:
         s = cpu_reference_seconds_per_image(gh, gw, make_layers(0), reps=1)
