@@ -213,6 +213,14 @@ typedef struct {
   float eps;       /* LayerNorm epsilon, 1e-6        */
   float rope_freq; /* 100                            */
   int math;        /* VK_MATH_BF16, VK_MATH_Q8_0 or VK_MATH_F32 */
+  /* Multi-view inputs (global cross-view layers, the reference's flash
+   * attention over views * tokens, src/specialized.rs:720-757): bit l of
+   * global_layers makes layer l attend across each group of `views`
+   * consecutive images (one sequence of views * tokens; RoPE positions repeat
+   * per view).  views <= 1 or global_layers == 0: every layer attends within
+   * its image.  With global layers, `images` must be a multiple of views. */
+  int views;
+  uint64_t global_layers;
 } vk_encoder_config;
 
 /* layers_host[cfg->layers], host f32 in the reference layout. */

@@ -549,7 +549,15 @@ void vko_encoder_layer(float* x, size_t tokens, size_t grid_h, size_t grid_w, si
   float* o = (float*)malloc(sizeof(float) * T * E);
   float* f = (float*)malloc(sizeof(float) * T * F);
   int64_t* pos = (int64_t*)malloc(sizeof(int64_t) * 2 * T);
+  /* tokens may span several views of one raster (global cross-view layers,
+   * src/specialized.rs:720-757): each view keeps its own RoPE positions and
+   * attention runs over all of them */
+  const size_t TV = grid_h * grid_w + 1;
   vko_da3_positions(grid_h, grid_w, pos);
+  for (size_t t = TV; t < T; ++t) {
+    pos[2 * t] = pos[2 * (t % TV)];
+    pos[2 * t + 1] = pos[2 * (t % TV) + 1];
+  }
 
   float* wqkv = copy_maybe_bf16(w->qkv_w, E * 3 * E, bf16_points);
   float* wo = copy_maybe_bf16(w->proj_w, E * E, bf16_points);

@@ -110,6 +110,9 @@ typedef struct {
   const float* ls2;             /* [E] */
 } vko_layer;
 
+/* tokens = views * (grid_h * grid_w + 1): with views > 1 the block attends
+ * across all views (a global cross-view layer); RoPE positions repeat per
+ * view. */
 void vko_encoder_layer(float* x, size_t tokens, size_t grid_h, size_t grid_w, size_t embed,
                        size_t heads, size_t ffn, const vko_layer* w, float eps, float rope_freq,
                        int bf16_points);

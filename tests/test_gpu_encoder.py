@@ -155,3 +155,39 @@ def test_large_batch_matches_single_images(vk, ctx, oracle_lib):
         one, _ = run_encoder(vk, ctx, layers, x[i:i + 1].copy(), 1, gh, gw, vk.MATH_BF16)
         err = rel_l2(big[i] - x[i], one[0] - x[i])
         assert err < 1e-3, (i, err)
+
+
+@pytest.mark.parametrize("math", ["bf16", "f32"])
+def test_multiview_global_layers(vk, ctx, oracle_lib, math):
+    """Layers 1 and 3 attend across each pair of views (one sequence of
+    2 x 25 tokens, RoPE positions repeating per view); layers 0 and 2 within
+    each view.  Oracle: the same composition from the restated block."""
+    gh, gw, V = 4, 6, 2
+    T = gh * gw + 1
+    layers = make_layers(4, 21, ls=0.1)
+    x = np.random.default_rng(22).standard_normal((4, T, E)).astype(np.float32)
+    m = {"bf16": vk.MATH_BF16, "f32": vk.MATH_F32}[math]
+    enc = vk.Encoder(ctx, layers, math=m, views=V, global_layers=(1, 3))
+    t = torch.from_numpy(x).cuda()
+    out = torch.empty_like(t)
+    assert enc.forward(t, out, 4, gh, gw)
+    ctx.synchronize()
+    got = out.cpu().numpy()
+    bf = math == "bf16"
+    for g in range(2):
+        views = [x[2 * g + i].copy() for i in range(V)]
+        for li, layer in enumerate(layers):
+            if li in (1, 3):
+                joint = oracle_lib.encoder_layer(np.concatenate(views), layer, gh, gw, bf16_points=bf)
+                views = [joint[i * T:(i + 1) * T] for i in range(V)]
+            else:
+                views = [oracle_lib.encoder_layer(v, layer, gh, gw, bf16_points=bf) for v in views]
+        for i in range(V):
+            img = 2 * g + i
+            err = rel_l2(got[img] - x[img], views[i] - x[img])
+            print(f"multi-view {math} image {img}: update rel_l2 {err:.2e}")
+            assert err < (1e-2 if bf else 1e-5)
+    # an image count that is not whole groups is refused, output untouched
+    out2 = torch.zeros((3, T, E), device="cuda")
+    assert not enc.forward(t[:3].contiguous(), out2, 3, gh, gw)
+    assert float(out2.abs().sum()) == 0.0

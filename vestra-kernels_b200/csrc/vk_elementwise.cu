@@ -192,7 +192,7 @@ cudaError_t layerscale_f32(float* x, size_t rows, size_t cols, const float* g, c
 // One thread per rotation pair.  rot[(t * 2 * quarter + axis * quarter + i) * 2 + {0: sin, 1: cos}]
 // as in src/rope.rs:49-60.  Products and sums are separately rounded (no FMA
 // contraction), so the result is bit-identical to the reference's rotate_half.
-__global__ void k_rope2d(float* x, int heads, int n, int head_dim, const float* __restrict__ rot) {
+__global__ void k_rope2d(float* x, int heads, int n, int head_dim, const float* __restrict__ rot, int period) {
   const int quarter = head_dim / 4, half = head_dim / 2;
   const size_t total = static_cast<size_t>(heads) * n * 2 * quarter;
   for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -200,7 +200,7 @@ __global__ void k_rope2d(float* x, int heads, int n, int head_dim, const float* 
     const int i = static_cast<int>(idx % quarter);
     const int axis = static_cast<int>((idx / quarter) % 2);
     const size_t ht = idx / (2 * quarter);  // h * n + p
-    const int p = static_cast<int>(ht % n);
+    const int p = static_cast<int>(ht % n) % period;  // rotation-table row
     float* base = x + ht * head_dim + axis * half;
     const float sn = rot[(static_cast<size_t>(p) * 2 * quarter + axis * quarter + i) * 2];
     const float cs = rot[(static_cast<size_t>(p) * 2 * quarter + axis * quarter + i) * 2 + 1];
@@ -209,10 +209,10 @@ __global__ void k_rope2d(float* x, int heads, int n, int head_dim, const float* 
     base[i + quarter] = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
   }
 }
-cudaError_t rope2d_f32(float* x, int heads, int n, int head_dim, const float* rot, cudaStream_t s) {
+cudaError_t rope2d_f32(float* x, int heads, int n, int head_dim, const float* rot, cudaStream_t s, int period) {
   const size_t total = static_cast<size_t>(heads) * n * (head_dim / 2);
   if (total == 0) return cudaSuccess;
-  k_rope2d<<<ew_grid(total), EW_THREADS, 0, s>>>(x, heads, n, head_dim, rot);
+  k_rope2d<<<ew_grid(total), EW_THREADS, 0, s>>>(x, heads, n, head_dim, rot, period > 0 ? period : n);
   return cudaGetLastError();
 }
 

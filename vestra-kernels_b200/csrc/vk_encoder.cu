@@ -132,6 +132,21 @@ int ensure_rope(vk_encoder* enc, size_t gh, size_t gw) {
 
 size_t rope_tokens(const vk_encoder* enc) { return enc->rope_h * enc->rope_w + 1; }
 
+// Images per attention sequence in layer li: cfg.views for a global
+// cross-view layer, else 1.
+size_t layer_views(const vk_encoder* enc, size_t li) {
+  const int v = enc->cfg.views;
+  if (v <= 1 || li >= 64 || ((enc->cfg.global_layers >> li) & 1u) == 0) return 1;
+  return static_cast<size_t>(v);
+}
+
+// Whether `images` splits into whole groups for every global layer.
+bool views_fit(const vk_encoder* enc, size_t images) {
+  for (size_t li = 0; li < enc->layers.size(); ++li)
+    if (images % layer_views(enc, li) != 0) return false;
+  return true;
+}
+
 // Enqueues one forward on `s`; returns the number of kernels launched or a
 // negative value on a launch error.
 int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const Acts& a, float* x, cudaStream_t s,
@@ -147,10 +162,18 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
     if ((expr) != cudaSuccess) return -1;               \
     ++launches;                                         \
   } while (0)
-  for (const EncLayer& L : enc->layers) {
+  for (size_t li = 0; li < enc->layers.size(); ++li) {
+    const EncLayer& L = enc->layers[li];
+    // A global cross-view layer attends over each group of `views`
+    // consecutive images as one sequence (src/specialized.rs:720-757);
+    // rows stay image-major, so only the attention's (images, tokens) and
+    // the head-major q / k / v layout change.  RoPE keeps per-view positions.
+    const size_t V = layer_views(enc, li);
+    const size_t ai = images / V, aT = T * V;
     GemmEpi qkv;
     qkv.bias = L.qkv_b;
-    qkv.tokens = static_cast<int>(T);
+    qkv.tokens = static_cast<int>(aT);
+    qkv.rope_tokens = static_cast<int>(T);
     qkv.heads = H;
     GemmEpi proj;
     proj.bias = L.proj_b;
@@ -170,7 +193,7 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
       fc1.out = a.h16;
       VK_L(layernorm_f32(x, nullptr, a.ln16, nullptr, nullptr, M, E, L.ln1_g, L.ln1_b, eps, s));
       VK_L(gemm_bf16_tc(a.ln16, L.qkv_w16, M, 3 * E, E, EPI_QKV_BF16, qkv, d_err, s));
-      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)images, H, (int)T, ATTN_OUT_TOKEN_BF16, a.att16, nullptr, d_err, s));
+      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)ai, H, (int)aT, ATTN_OUT_TOKEN_BF16, a.att16, nullptr, d_err, s));
       VK_L(gemm_bf16_tc(a.att16, L.proj_w16, M, E, E, EPI_RESID, proj, d_err, s));
       VK_L(layernorm_f32(x, nullptr, a.ln16, nullptr, nullptr, M, E, L.ln2_g, L.ln2_b, eps, s));
       VK_L(gemm_bf16_tc(a.ln16, L.fc1_w16, M, F, E, EPI_BF16_GELU, fc1, d_err, s));
@@ -181,7 +204,7 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
       fc1.q8d = a.hd;
       VK_L(layernorm_f32(x, nullptr, nullptr, a.lnq, a.lnd, M, E, L.ln1_g, L.ln1_b, eps, s));
       VK_L(gemm_q8_tc(a.lnq, a.lnd, L.qkv_q, L.qkv_d, M, 3 * E, E, EPI_QKV_BF16, qkv, nullptr, d_err, s));
-      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)images, H, (int)T, ATTN_OUT_TOKEN_Q8, a.attq, a.attd, d_err, s));
+      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)ai, H, (int)aT, ATTN_OUT_TOKEN_Q8, a.attq, a.attd, d_err, s));
       VK_L(gemm_q8_tc(a.attq, a.attd, L.proj_q, L.proj_d, M, E, E, EPI_RESID, proj, nullptr, d_err, s));
       VK_L(layernorm_f32(x, nullptr, nullptr, a.lnq, a.lnd, M, E, L.ln2_g, L.ln2_b, eps, s));
       VK_L(gemm_q8_tc(a.lnq, a.lnd, L.fc1_q, L.fc1_d, M, F, E, EPI_Q8_GELU, fc1, nullptr, d_err, s));
@@ -191,10 +214,10 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
       fc1.out = a.h32;
       VK_L(layernorm_f32(x, a.ln32, nullptr, nullptr, nullptr, M, E, L.ln1_g, L.ln1_b, eps, s));
       VK_L(gemm_f32_simt(a.ln32, L.qkv_w32, M, 3 * E, E, EPI_QKV_F32, qkv, s));
-      VK_L(rope2d_f32(a.q32, (int)images * H, (int)T, 64, enc->rope, s));
-      VK_L(rope2d_f32(a.k32, (int)images * H, (int)T, 64, enc->rope, s));
-      VK_L(attention_f32(a.q32, a.k32, a.v32, (int)images * H, (int)T, 64, a.att32, s));
-      VK_L(hnd_to_token_f32(a.att32, a.tok32, (int)images, H, (int)T, s));
+      VK_L(rope2d_f32(a.q32, (int)ai * H, (int)aT, 64, enc->rope, s, (int)T));
+      VK_L(rope2d_f32(a.k32, (int)ai * H, (int)aT, 64, enc->rope, s, (int)T));
+      VK_L(attention_f32(a.q32, a.k32, a.v32, (int)ai * H, (int)aT, 64, a.att32, s));
+      VK_L(hnd_to_token_f32(a.att32, a.tok32, (int)ai, H, (int)aT, s));
       VK_L(gemm_f32_simt(a.tok32, L.proj_w32, M, E, E, EPI_RESID, proj, s));
       VK_L(layernorm_f32(x, a.ln32, nullptr, nullptr, nullptr, M, E, L.ln2_g, L.ln2_b, eps, s));
       VK_L(gemm_f32_simt(a.ln32, L.fc1_w32, M, F, E, EPI_F32_GELU, fc1, s));
@@ -232,6 +255,7 @@ extern "C" int vk_encoder_prepare(vk_ctx* ctx, const vk_encoder_config* cfg, con
   if (!ctx || !cfg || !layers_host || !out) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_prepare: NULL argument");
   *out = nullptr;
   cudaSetDevice(ctx->device);
+  if (cfg->views < 0) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_prepare: negative views");
   if (cfg->layers <= 0 || cfg->heads <= 0 || cfg->ffn <= 0)
     return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_prepare: empty configuration");
   const int E = cfg->heads * 64, F = cfg->ffn;
@@ -344,6 +368,9 @@ extern "C" int vk_encoder_forward(vk_ctx* ctx, vk_encoder* enc, size_t images, s
     for (cudaEvent_t ev : enc->slot_out)
       if (ev) VK_TRY_CUDA(cudaStreamWaitEvent(ctx->stream, ev, 0), "vk_encoder_forward ordering");
   }
+  if (!views_fit(enc, images))
+    return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_forward: %zu images are not whole groups of %d views", images,
+                   enc->cfg.views);
   VK_TRY(forward_on_stream(ctx, enc, images, grid_h, grid_w, tokens_dev, out_dev, ctx->stream));
   if (enc->dev_tail) VK_TRY_CUDA(cudaEventRecord(enc->dev_tail, ctx->stream), "vk_encoder_forward ordering");
   return VK_OK;
@@ -359,6 +386,9 @@ static int host_pipeline(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t gri
   cudaSetDevice(ctx->device);
   if (images == 0) return VK_OK;
   if (grid_h == 0 || grid_w == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "%s: empty patch grid", name);
+  if (!views_fit(enc, images))
+    return vk_fail(VK_UNSUPPORTED_SHAPE, "%s: %zu images are not whole groups of %d views", name, images,
+                   enc->cfg.views);
   const size_t T = grid_h * grid_w + 1, E = enc->embed;
   // A waiting call overlaps copies with compute only inside itself, so it
   // cuts the batch into 16-image chunks; back-to-back asynchronous calls
@@ -367,6 +397,8 @@ static int host_pipeline(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t gri
   size_t chunk = wait ? 16 : 64;
   if (const char* c = getenv("VK_E2E_CHUNK")) chunk = static_cast<size_t>(atoi(c));
   if (chunk == 0 || chunk > images) chunk = images;
+  if (enc->cfg.views > 1) chunk = (chunk + enc->cfg.views - 1) / enc->cfg.views * enc->cfg.views;  // whole groups
+  if (chunk > images) chunk = images;
   const size_t rows = chunk * T;
   if (!enc->comp) {
     for (cudaStream_t* st : {&enc->comp, &enc->h2d, &enc->d2h})
@@ -428,6 +460,7 @@ extern "C" int vk_encoder_profile(vk_ctx* ctx, vk_encoder* enc, size_t images, s
     return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_profile: NULL argument");
   cudaSetDevice(ctx->device);
   if (images == 0 || grid_h == 0 || grid_w == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_profile: empty shape");
+  if (!views_fit(enc, images)) return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_profile: images not whole view groups");
   const size_t T = grid_h * grid_w + 1, M = images * T;
   Acts a;
   VK_TRY(ensure_acts(enc, M, a));

@@ -70,10 +70,13 @@ __device__ __forceinline__ void epi_math(const GemmEpi& p, int row, int col0, fl
     if (p.rope != nullptr && q.g < 2) {
       // Axial RoPE, rotate-half pairing (i, i + 16) inside this 32-wide axis
       // half (src/rope.rs:84-93); the chunk is exactly one axis half.
-      const float4* r = reinterpret_cast<const float4*>(p.rope) + static_cast<size_t>(q.axis * 8) * p.tokens + q.t;
+      // a global cross-view layer's token t sits at view position t % rope_tokens
+      const int rt = p.rope_tokens > 0 ? p.rope_tokens : p.tokens;
+      const int tr = p.rope_tokens > 0 ? q.t % p.rope_tokens : q.t;
+      const float4* r = reinterpret_cast<const float4*>(p.rope) + static_cast<size_t>(q.axis * 8) * rt + tr;
 #pragma unroll
       for (int i2 = 0; i2 < 8; ++i2) {
-        const float4 sc = __ldg(r + static_cast<size_t>(i2) * p.tokens);  // (sin, cos) of 2 i2, 2 i2 + 1
+        const float4 sc = __ldg(r + static_cast<size_t>(i2) * rt);  // (sin, cos) of 2 i2, 2 i2 + 1
         const int i = 2 * i2;
         const float a0 = v[i], b0 = v[i + 16], a1 = v[i + 1], b1 = v[i + 17];
         v[i] = a0 * sc.y - b0 * sc.x;

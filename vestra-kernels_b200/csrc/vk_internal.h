@@ -34,7 +34,8 @@ struct GemmEpi {
   void* k = nullptr;
   void* v = nullptr;
   const float* rope = nullptr;   // [2 * 8, tokens] of (sin_i, cos_i, sin_i+1, cos_i+1): [axis * 8 + i / 2][t], or null
-  int tokens = 0;                // rows per image
+  int tokens = 0;                // rows per image (per group of views for a global layer)
+  int rope_tokens = 0;           // rows of the rotation table (0: tokens); token t uses row t % rope_tokens
   int heads = 0;                 // embed = heads * 64
   int8_t* q8 = nullptr;          // [M, N] int8 quants (EPI_Q8_GELU)
   __half* q8d = nullptr;         // [M, N / 32] scales
@@ -80,7 +81,8 @@ cudaError_t add_bias_rows_f32(float* x, size_t rows, size_t cols, const float* b
                               cudaStream_t s);
 cudaError_t layerscale_f32(float* x, size_t rows, size_t cols, const float* g, cudaStream_t s);
 cudaError_t rope2d_f32(float* x, int heads, int n, int head_dim, const float* rot,
-                       cudaStream_t s);
+                       cudaStream_t s,
+                       int period = 0);  // rows of `rot` (0: n); token p uses row p % period
 cudaError_t qk_norm_rope_f32(float* q, float* k, int heads, int tokens, const float* qg,
                              const float* qb, const float* kg, const float* kb, const float* rot,
                              float eps, cudaStream_t s);

@@ -399,7 +399,8 @@ class _LayerWeights(ctypes.Structure):
 
 class _EncoderConfig(ctypes.Structure):
     _fields_ = [("layers", ctypes.c_int), ("heads", ctypes.c_int), ("ffn", ctypes.c_int),
-                ("eps", ctypes.c_float), ("rope_freq", ctypes.c_float), ("math", ctypes.c_int)]
+                ("eps", ctypes.c_float), ("rope_freq", ctypes.c_float), ("math", ctypes.c_int),
+                ("views", ctypes.c_int), ("global_layers", ctypes.c_uint64)]
 
 
 LAYER_KEYS = ["ln1_g", "ln1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ls1",
@@ -411,7 +412,9 @@ class Encoder:
     keyed by LAYER_KEYS in the reference layout ([K, N] weights)."""
 
     def __init__(self, ctx: Context, layers, heads: int = 12, ffn: int = 3072, eps: float = 1e-6,
-                 rope_freq: float = 100.0, math: int = MATH_BF16):
+                 rope_freq: float = 100.0, math: int = MATH_BF16, views: int = 1, global_layers=()):
+        """views / global_layers: layers listed in global_layers attend across
+        each group of `views` consecutive images (multi-view global attention)."""
         import numpy as np
 
         self.ctx = ctx
@@ -423,16 +426,23 @@ class Encoder:
             keep.append(vals)
             for fname, arr in zip((f for f, _ in _LayerWeights._fields_), vals):
                 setattr(structs[i], fname, arr.ctypes.data)
-        cfg = _EncoderConfig(len(layers), heads, ffn, eps, rope_freq, math)
+        mask = 0
+        for li in global_layers:
+            if not 0 <= li < min(len(layers), 64):
+                raise ValueError(f"global layer {li} outside 0..{len(layers) - 1}")
+            mask |= 1 << li
+        cfg = _EncoderConfig(len(layers), heads, ffn, eps, rope_freq, math, views, mask)
         h = ctypes.c_void_p()
         st = _check(lib().vk_encoder_prepare(ctx.handle, ctypes.byref(cfg), structs, ctypes.byref(h)))
         if st != VK_OK:
             raise VestraError(st, last_error())
         self.handle = h
 
-    def forward(self, tokens, out, images: int, grid_h: int, grid_w: int) -> None:
-        """Device tensors [images, 1 + grid_h * grid_w, E] f32 (may alias)."""
-        _check(lib().vk_encoder_forward(self.ctx.handle, self.handle, images, grid_h, grid_w, _ptr(tokens), _ptr(out)))
+    def forward(self, tokens, out, images: int, grid_h: int, grid_w: int) -> bool:
+        """Device tensors [images, 1 + grid_h * grid_w, E] f32 (may alias); False
+        (output untouched) for an unsupported shape."""
+        return _check(lib().vk_encoder_forward(self.ctx.handle, self.handle, images, grid_h, grid_w, _ptr(tokens),
+                                               _ptr(out))) == VK_OK
 
     def forward_host(self, tokens, out, images: int, grid_h: int, grid_w: int) -> None:
         """Host tensors (pinned for overlap); copies are pipelined with compute."""
