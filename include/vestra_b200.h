@@ -204,6 +204,10 @@ typedef struct {
   const float *fc1_weight, *fc1_bias;    /* [E, F], [F]    */
   const float *fc2_weight, *fc2_bias;    /* [F, E], [E]    */
   const float* ls2;                      /* [E]            */
+  /* Optional Q/K LayerNorm before RoPE (DA3's late blocks;
+   * qk_norm_rope_f32_da3_base, src/specialized.rs:278-454): [64] each, all
+   * four set or all NULL; eps = the encoder's eps.  bf16 and f32 math. */
+  const float *q_norm_gamma, *q_norm_beta, *k_norm_gamma, *k_norm_beta;
 } vk_layer_weights;
 
 typedef struct {

@@ -265,13 +265,22 @@ def prepend_cls_add_pos(patches, cls, position, patch_count, embed) -> np.ndarra
     return out
 
 
+LAYER_KEYS = ["ln1_g", "ln1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ls1",
+              "ln2_g", "ln2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "ls2"]
+# optional Q/K LayerNorm vectors of a layer dict -> struct fields
+QK_NORM_KEYS = {"q_norm_g": "qn_g", "q_norm_b": "qn_b", "k_norm_g": "kn_g", "k_norm_b": "kn_b"}
+
+
 class _Layer(ctypes.Structure):
-    _fields_ = [(n, _f) for n in (
-        "ln1_g", "ln1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ls1",
-        "ln2_g", "ln2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "ls2")]
+    _fields_ = [(n, _f) for n in LAYER_KEYS + list(QK_NORM_KEYS.values())]
 
 
-LAYER_KEYS = [n for n, _ in _Layer._fields_]
+def _layer_struct(layer: dict):
+    keep = {kk: _f32(layer[kk]) for kk in LAYER_KEYS}
+    for kk, field in QK_NORM_KEYS.items():
+        if layer.get(kk) is not None:
+            keep[field] = _f32(layer[kk])
+    return keep, _Layer(**{kk: _p(vv) for kk, vv in keep.items()})
 
 
 def encoder_layer(x, layer: dict, grid_h, grid_w, heads=12, eps=1e-6, freq=100.0, bf16_points=False):
@@ -279,8 +288,7 @@ def encoder_layer(x, layer: dict, grid_h, grid_w, heads=12, eps=1e-6, freq=100.0
     x = _f32(x).copy()
     t, e = x.shape
     ffn = np.shape(layer["fc1_w"])[1]
-    keep = {kk: _f32(layer[kk]) for kk in LAYER_KEYS}
-    st = _Layer(**{kk: _p(vv) for kk, vv in keep.items()})
+    keep, st = _layer_struct(layer)
     lib().vko_encoder_layer(_p(x), _sz(t), _sz(grid_h), _sz(grid_w), _sz(e), _sz(heads), _sz(ffn),
                             ctypes.byref(st), ctypes.c_float(eps), ctypes.c_float(freq),
                             ctypes.c_int(1 if bf16_points else 0))
@@ -312,8 +320,7 @@ def cpu_ref():
 def cpu_ref_encoder_layer(x, layer: dict, grid_h, grid_w, eps=1e-6, freq=100.0):
     """One block on the restated AVX-512 path; x [T, 768], modified copy returned."""
     x = _f32(x).copy()
-    keep = {kk: _f32(layer[kk]) for kk in LAYER_KEYS}
-    st = _Layer(**{kk: _p(vv) for kk, vv in keep.items()})
+    keep, st = _layer_struct(layer)
     cpu_ref().vkr_encoder_layer(_p(x), _sz(x.shape[0]), _sz(grid_h), _sz(grid_w), ctypes.byref(st),
                                 ctypes.c_float(eps), ctypes.c_float(freq))
     return x

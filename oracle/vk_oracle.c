@@ -568,8 +568,12 @@ void vko_encoder_layer(float* x, size_t tokens, size_t grid_h, size_t grid_w, si
   vko_layernorm(h, T, E, w->ln1_g, w->ln1_b, eps);
   if (bf16_points) round_bf16_buf(h, T * E);
   vko_qkv(T, heads, h, wqkv, w->qkv_b, q, k, v);
-  vko_rope2d(q, heads, T, 64, pos, rope_freq);
-  vko_rope2d(k, heads, T, 64, pos, rope_freq);
+  if (w->qn_g != NULL) {
+    vko_qk_norm_rope(q, k, heads, T, w->qn_g, w->qn_b, w->kn_g, w->kn_b, pos, rope_freq, eps);
+  } else {
+    vko_rope2d(q, heads, T, 64, pos, rope_freq);
+    vko_rope2d(k, heads, T, 64, pos, rope_freq);
+  }
   if (bf16_points) {
     round_bf16_buf(q, T * E);
     round_bf16_buf(k, T * E);

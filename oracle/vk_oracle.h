@@ -108,6 +108,9 @@ typedef struct {
   const float *fc1_w, *fc1_b;   /* [E, F], [F] */
   const float *fc2_w, *fc2_b;   /* [F, E], [E] */
   const float* ls2;             /* [E] */
+  /* optional Q/K LayerNorm before RoPE (qk_norm_rope_f32_da3_base,
+   * src/specialized.rs:278-454): [64] each, or all NULL */
+  const float *qn_g, *qn_b, *kn_g, *kn_b;
 } vko_layer;
 
 /* tokens = views * (grid_h * grid_w + 1): with views > 1 the block attends

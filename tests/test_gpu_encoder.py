@@ -191,3 +191,54 @@ def test_multiview_global_layers(vk, ctx, oracle_lib, math):
     out2 = torch.zeros((3, T, E), device="cuda")
     assert not enc.forward(t[:3].contiguous(), out2, 3, gh, gw)
     assert float(out2.abs().sum()) == 0.0
+
+
+def add_qk_norm(layer, seed):
+    r = np.random.default_rng(seed)
+    layer = dict(layer)
+    layer["q_norm_g"] = (1.0 + 0.1 * r.standard_normal(64)).astype(np.float32)
+    layer["q_norm_b"] = (0.05 * r.standard_normal(64)).astype(np.float32)
+    layer["k_norm_g"] = (1.0 + 0.1 * r.standard_normal(64)).astype(np.float32)
+    layer["k_norm_b"] = (0.05 * r.standard_normal(64)).astype(np.float32)
+    return layer
+
+
+@pytest.mark.parametrize("math", ["bf16", "f32"])
+def test_qk_norm_layers(vk, ctx, oracle_lib, math):
+    """Layers 1 and 2 LayerNorm each q / k head before RoPE (DA3's late
+    blocks, qk_norm_rope_f32_da3_base); layer 2 is also a global cross-view
+    layer.  Oracle: the restated block with the same options."""
+    gh, gw, V = 4, 6, 2
+    T = gh * gw + 1
+    layers = make_layers(3, 31, ls=0.1)
+    layers[1] = add_qk_norm(layers[1], 32)
+    layers[2] = add_qk_norm(layers[2], 33)
+    x = np.random.default_rng(34).standard_normal((2, T, E)).astype(np.float32)
+    m = {"bf16": vk.MATH_BF16, "f32": vk.MATH_F32}[math]
+    enc = vk.Encoder(ctx, layers, math=m, views=V, global_layers=(2,))
+    t = torch.from_numpy(x).cuda()
+    out = torch.empty_like(t)
+    assert enc.forward(t, out, 2, gh, gw)
+    ctx.synchronize()
+    got = out.cpu().numpy()
+    bf = math == "bf16"
+    views = [x[0].copy(), x[1].copy()]
+    for li, layer in enumerate(layers):
+        if li == 2:
+            joint = oracle_lib.encoder_layer(np.concatenate(views), layer, gh, gw, bf16_points=bf)
+            views = [joint[:T], joint[T:]]
+        else:
+            views = [oracle_lib.encoder_layer(v, layer, gh, gw, bf16_points=bf) for v in views]
+    for i in range(2):
+        err = rel_l2(got[i] - x[i], views[i] - x[i])
+        print(f"qk-norm {math} image {i}: update rel_l2 {err:.2e}")
+        assert err < (1e-2 if bf else 1e-5)
+    slots = enc.profile(t, out, 2, gh, gw)
+    assert len(slots) == (10 if math == "f32" else 7) and all(s >= 0.0 for s in slots)
+
+
+def test_qk_norm_needs_bf16_or_f32(vk, ctx):
+    layers = make_layers(1, 35)
+    layers[0] = add_qk_norm(layers[0], 36)
+    with pytest.raises(vk.VestraError):
+        vk.Encoder(ctx, layers, math=vk.MATH_Q8_0)

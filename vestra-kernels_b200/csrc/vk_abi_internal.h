@@ -53,6 +53,7 @@ struct EncLayer {
   __nv_bfloat16 *qkv_w16, *proj_w16, *fc1_w16, *fc2_w16;  // [N, K]
   int8_t *qkv_q, *proj_q, *fc1_q, *fc2_q;                 // [N, K]
   __half *qkv_d, *proj_d, *fc1_d, *fc2_d;                 // [N, K / 32]
+  float* qkn;  // [4][64]: q gamma, q beta, k gamma, k beta (Q/K LayerNorm before RoPE), or null
 };
 
 struct vk_encoder {

@@ -175,6 +175,8 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
     qkv.tokens = static_cast<int>(aT);
     qkv.rope_tokens = static_cast<int>(T);
     qkv.heads = H;
+    qkv.qkn = L.qkn;
+    qkv.qkn_eps = eps;
     GemmEpi proj;
     proj.bias = L.proj_b;
     proj.scale = L.ls1;
@@ -214,8 +216,13 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
       fc1.out = a.h32;
       VK_L(layernorm_f32(x, a.ln32, nullptr, nullptr, nullptr, M, E, L.ln1_g, L.ln1_b, eps, s));
       VK_L(gemm_f32_simt(a.ln32, L.qkv_w32, M, 3 * E, E, EPI_QKV_F32, qkv, s));
-      VK_L(rope2d_f32(a.q32, (int)ai * H, (int)aT, 64, enc->rope, s, (int)T));
-      VK_L(rope2d_f32(a.k32, (int)ai * H, (int)aT, 64, enc->rope, s, (int)T));
+      if (L.qkn != nullptr) {  // rows of [ai * H, aT, 64]; the table row is row % T
+        VK_L(qk_norm_rope_f32(a.q32, a.k32, (int)(ai * H * (aT / T)), (int)T, L.qkn, L.qkn + 64, L.qkn + 128,
+                              L.qkn + 192, enc->rope, eps, s));
+      } else {
+        VK_L(rope2d_f32(a.q32, (int)ai * H, (int)aT, 64, enc->rope, s, (int)T));
+        VK_L(rope2d_f32(a.k32, (int)ai * H, (int)aT, 64, enc->rope, s, (int)T));
+      }
       VK_L(attention_f32(a.q32, a.k32, a.v32, (int)ai * H, (int)aT, 64, a.att32, s));
       VK_L(hnd_to_token_f32(a.att32, a.tok32, (int)ai, H, (int)aT, s));
       VK_L(gemm_f32_simt(a.tok32, L.proj_w32, M, E, E, EPI_RESID, proj, s));
@@ -290,6 +297,22 @@ extern "C" int vk_encoder_prepare(vk_ctx* ctx, const vk_encoder_config* cfg, con
     if (st == VK_OK) st = vec(w.fc1_bias, F, &L.fc1_b);
     if (st == VK_OK) st = vec(w.fc2_bias, E, &L.fc2_b);
     if (st == VK_OK) st = vec(w.ls2, E, &L.ls2);
+    const int nq = (w.q_norm_gamma != nullptr) + (w.q_norm_beta != nullptr) + (w.k_norm_gamma != nullptr) +
+                   (w.k_norm_beta != nullptr);
+    if (st == VK_OK && nq != 0 && nq != 4)
+      st = vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_prepare: layer %d sets only some Q/K norm vectors", l);
+    if (st == VK_OK && nq == 4 && cfg->math == VK_MATH_Q8_0)
+      st = vk_fail(VK_UNSUPPORTED_SHAPE, "vk_encoder_prepare: Q/K LayerNorm needs bf16 or f32 math");
+    if (st == VK_OK && nq == 4) {
+      float qkn[256];
+      for (int i = 0; i < 64; ++i) {
+        qkn[i] = w.q_norm_gamma[i];
+        qkn[64 + i] = w.q_norm_beta[i];
+        qkn[128 + i] = w.k_norm_gamma[i];
+        qkn[192 + i] = w.k_norm_beta[i];
+      }
+      st = vec(qkn, 256, &L.qkn);
+    }
     if (st == VK_OK && (!w.qkv_weight || !w.proj_weight || !w.fc1_weight || !w.fc2_weight))
       st = vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_prepare: NULL layer weight");
     if (st == VK_OK)
@@ -467,7 +490,13 @@ extern "C" int vk_encoder_profile(vk_ctx* ctx, vk_encoder* enc, size_t images, s
   VK_TRY(ensure_rope(enc, grid_h, grid_w));
   const int per_layer = enc->cfg.math == VK_MATH_F32 ? 10 : 7;
   if (slots < per_layer) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_encoder_profile: need %d slots", per_layer);
-  const int total = per_layer * enc->cfg.layers;
+  // launch i of the forward -> (slot); an f32 layer with Q/K LayerNorm runs
+  // one fused norm + RoPE kernel in the two RoPE slots (it is booked to the first)
+  std::vector<int> slot_of;
+  for (const EncLayer& L : enc->layers)
+    for (int j = 0; j < per_layer; ++j)
+      if (!(enc->cfg.math == VK_MATH_F32 && L.qkn != nullptr && j == 3)) slot_of.push_back(j);
+  const int total = static_cast<int>(slot_of.size());
   std::vector<cudaEvent_t> evs(total + 1);
   for (auto& e : evs) VK_TRY_CUDA(cudaEventCreate(&e), "profile event");
   if (tokens_dev != out_dev)
@@ -480,7 +509,7 @@ extern "C" int vk_encoder_profile(vk_ctx* ctx, vk_encoder* enc, size_t images, s
     for (int i = 0; i < n; ++i) {
       float ms = 0.0f;
       cudaEventElapsedTime(&ms, evs[i], evs[i + 1]);
-      ms_per_slot[i % per_layer] += ms;
+      ms_per_slot[slot_of[i]] += ms;
     }
   for (auto& ev : evs) cudaEventDestroy(ev);
   if (e != cudaSuccess) return vk_cuda_status(e, "vk_encoder_profile");

@@ -126,6 +126,65 @@ __device__ __forceinline__ void epilogue_part(const GemmEpi& epi, const CUtensor
     if (lane == 0) bulk_wait_read<0>();  // the previous tile's stores are done with the slice
     __syncwarp();
   }
+  if constexpr (MODE == EPI_QKV_BF16) {
+    if (epi.qkn != nullptr) {
+      // Q/K LayerNorm before RoPE (src/specialized.rs:278-454): the two
+      // 32-column chunks of a head (both RoPE axis halves) belong to this
+      // thread, so the 64-wide row is normalised in registers.
+#pragma unroll 1
+      for (int cp = 0; cp < NCOL / 64; ++cp) {
+        float v[64];
+        tmem_ld32(tbase + static_cast<uint32_t>(cp * 64), *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(tbase + static_cast<uint32_t>(cp * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
+        if (cp + 1 == NCOL / 64) release();
+        if (row0 >= M) continue;
+        const int col0 = c0 + cp * 64;
+        if (sbias != nullptr)
+#pragma unroll
+          for (int d = 0; d < 64; ++d) v[d] += sbias[cp * 64 + d];
+        const QkvPos q = qkv_pos(epi, row, col0);
+        if (q.g < 2) {
+          const float* gm = epi.qkn + q.g * 128;  // gamma, then beta
+          float sum = 0.0f;
+#pragma unroll
+          for (int d = 0; d < 64; ++d) sum += v[d];
+          const float mean = sum / 64.0f;
+          float sq = 0.0f;
+#pragma unroll
+          for (int d = 0; d < 64; ++d) {
+            const float dv = v[d] - mean;
+            sq = fmaf(dv, dv, sq);
+          }
+          const float inv = 1.0f / sqrtf(sq / 64.0f + epi.qkn_eps);
+#pragma unroll
+          for (int d = 0; d < 64; ++d) v[d] = (v[d] - mean) * inv * __ldg(gm + d) + __ldg(gm + 64 + d);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float(&half)[32] = *reinterpret_cast<float(*)[32]>(&v[32 * h]);
+          epi_math<MODE, true>(epi, row, col0 + 32 * h, half, nullptr, nullptr);  // RoPE on q / k
+          if (direct) {
+            if (row < M) epi_direct<MODE>(epi, row, col0 + 32 * h, N, half);
+          } else {
+            stage_row<false>(stage + (2 * cp + h) * OUT_BUF, lane, half);
+            staged = true;
+          }
+        }
+      }
+      if (staged) {
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+          for (int c = 0; c < NCOL / 32; ++c)
+            store_chunk<MODE>(epi, tmO0, tmO1, tmO2, stage + c * OUT_BUF, row0, c0 + c * 32, img, t0);
+          bulk_commit();
+        }
+      }
+      return;
+    }
+  }
   uint32_t r[2][32];
   tmem_ld32(tbase, r[0]);
 #pragma unroll

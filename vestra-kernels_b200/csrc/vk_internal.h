@@ -37,6 +37,8 @@ struct GemmEpi {
   int tokens = 0;                // rows per image (per group of views for a global layer)
   int rope_tokens = 0;           // rows of the rotation table (0: tokens); token t uses row t % rope_tokens
   int heads = 0;                 // embed = heads * 64
+  const float* qkn = nullptr;    // [4][64] q gamma, q beta, k gamma, k beta: LayerNorm of each q / k head before RoPE, or null
+  float qkn_eps = 0.0f;
   int8_t* q8 = nullptr;          // [M, N] int8 quants (EPI_Q8_GELU)
   __half* q8d = nullptr;         // [M, N / 32] scales
 };

@@ -394,7 +394,8 @@ class PatchEmbed:
 class _LayerWeights(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in (
         "ln1_gamma", "ln1_beta", "qkv_weight", "qkv_bias", "proj_weight", "proj_bias", "ls1",
-        "ln2_gamma", "ln2_beta", "fc1_weight", "fc1_bias", "fc2_weight", "fc2_bias", "ls2")]
+        "ln2_gamma", "ln2_beta", "fc1_weight", "fc1_bias", "fc2_weight", "fc2_bias", "ls2",
+        "q_norm_gamma", "q_norm_beta", "k_norm_gamma", "k_norm_beta")]
 
 
 class _EncoderConfig(ctypes.Structure):
@@ -405,6 +406,8 @@ class _EncoderConfig(ctypes.Structure):
 
 LAYER_KEYS = ["ln1_g", "ln1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ls1",
               "ln2_g", "ln2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "ls2"]
+# optional per layer: Q/K LayerNorm before RoPE ([64] each; all four or none)
+QK_NORM_KEYS = ["q_norm_g", "q_norm_b", "k_norm_g", "k_norm_b"]
 
 
 class Encoder:
@@ -423,9 +426,11 @@ class Encoder:
         keep, structs = [], (_LayerWeights * len(layers))()
         for i, layer in enumerate(layers):
             vals = [np.ascontiguousarray(layer[kk], dtype=np.float32) for kk in LAYER_KEYS]
+            vals += [None if layer.get(kk) is None else np.ascontiguousarray(layer[kk], dtype=np.float32)
+                     for kk in QK_NORM_KEYS]
             keep.append(vals)
             for fname, arr in zip((f for f, _ in _LayerWeights._fields_), vals):
-                setattr(structs[i], fname, arr.ctypes.data)
+                setattr(structs[i], fname, None if arr is None else arr.ctypes.data)
         mask = 0
         for li in global_layers:
             if not 0 <= li < min(len(layers), 64):
