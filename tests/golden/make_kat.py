@@ -29,6 +29,14 @@ KAT = {
         "bias": [1.0, -4.0], "gamma": [0.5, 2.0],
         "epilogue": [29.5, 120.0, 70.0, 300.0],
     },
+    "cuda.prepared_linear_chain": {
+        "source": "src/cuda.rs:1433-1447",
+        "left": [1.0, 2.0, 3.0, 4.0, 5.0, 6.0], "rows": 2,
+        "first": {"k": 3, "n": 2, "weight": [7.0, 8.0, 9.0, 10.0, 11.0, 12.0], "bias": [1.0, -4.0],
+                  "scale": [0.5, 2.0]},
+        "second": {"k": 2, "n": 1, "weight": [2.0, -1.0], "bias": [3.0]},
+        "expected": [-58.0, -157.0],
+    },
     "cuda.add": {
         "source": "src/cuda.rs:1375-1381",
         "a": [1.0, -2.0, 3.5], "b": [0.5, 2.0, -1.0], "expected": [1.5, 0.0, 2.5],

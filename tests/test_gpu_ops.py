@@ -183,6 +183,25 @@ def test_linear_rejects_non_da3_shape(vk, ctx):
     assert float(out.abs().sum()) == 0.0
 
 
+def test_prepared_linear_chain_matches_reference_values(vk, ctx):
+    """src/cuda.rs:1433-1447: two prepared linears run back to back (f32)."""
+    import json
+    import os
+
+    with open(os.path.join(os.path.dirname(__file__), "golden", "reference_kat.json")) as fh:
+        case = json.load(fh)["cuda.prepared_linear_chain"]
+    f, g = case["first"], case["second"]
+    first = vk.Linear(ctx, np.array(f["weight"], np.float32).reshape(f["k"], f["n"]), f["bias"], f["scale"],
+                      math=vk.MATH_F32)
+    second = vk.Linear(ctx, np.array(g["weight"], np.float32).reshape(g["k"], g["n"]), g["bias"], None,
+                       math=vk.MATH_F32)
+    mid = torch.empty(case["rows"] * f["n"], device="cuda")
+    out = torch.empty(case["rows"] * g["n"], device="cuda")
+    first(dev(np.array(case["left"], np.float32)), mid)
+    second(mid, out)
+    assert host(out).tolist() == case["expected"]
+
+
 def test_prepared_linear_matches_raw(vk, ctx, oracle_lib):
     x, w, b, s = rng_inputs(60, (300, 768), (768, 768), (768,), (768,))
     w *= np.float32(0.02)

@@ -165,3 +165,4 @@ def test_patch_embed_rejects_non_multiple_grid(vk, ctx):
     out = torch.zeros((1, 5, 768), device="cuda")
     assert not pe(torch.zeros(3 * 30 * 28, device="cuda"), dev(pos), out, 1, 30, 28)
     assert float(out.abs().sum()) == 0.0
+

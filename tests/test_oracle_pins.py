@@ -67,6 +67,17 @@ def test_cuda_module_gemm_and_bias_scale_values(oracle_lib, kat):
     assert c.ravel().tolist() == case["epilogue"]
 
 
+def test_cuda_module_prepared_linear_chain(oracle_lib, kat):
+    case = kat["cuda.prepared_linear_chain"]
+    left = np.array(case["left"], np.float32).reshape(case["rows"], -1)
+    f, g = case["first"], case["second"]
+    h = oracle_lib.linear_bias_scale(left, np.array(f["weight"], np.float32).reshape(f["k"], f["n"]), f["bias"],
+                                     f["scale"])
+    out = oracle_lib.linear_bias_scale(h, np.array(g["weight"], np.float32).reshape(g["k"], g["n"]), g["bias"],
+                                       np.ones(g["n"], np.float32))
+    assert out.ravel().tolist() == case["expected"]
+
+
 def test_cuda_module_patchify_values(oracle_lib, kat):
     case = kat["cuda.patchify_nchw"]
     image = np.arange(48, dtype=np.float32)
