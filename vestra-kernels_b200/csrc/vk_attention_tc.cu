@@ -360,13 +360,8 @@ __global__ void __launch_bounds__(A_THREADS, 1)
 template <int OUT>
 static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int images,
                                int heads, int tokens, void* out, __half* q8d, int* err, cudaStream_t s) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_attention_tc<OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(ATT_SMEM));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(k_attention_tc<OUT>), static_cast<int>(ATT_SMEM));
+  if (e != cudaSuccess) return e;
   const int items = ((tokens + 2 * AQ - 1) / (2 * AQ)) * images * heads;
   const int grid = items < num_sms() ? items : num_sms();
   cudaLaunchConfig_t cfg = {};

@@ -242,8 +242,7 @@ template <int MODE, bool DUMP>
 static cudaError_t launch_q8(const CUtensorMap& ta, const CUtensorMap& tb, const __half* Ad, const __half* Wd,
                              const GemmEpi& epi, int M, int N, int K, int32_t* dots, int* err, cudaStream_t s) {
   const size_t smem = q8_smem_bytes(K);
-  cudaError_t e = cudaFuncSetAttribute(k_gemm_q8<MODE, DUMP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(k_gemm_q8<MODE, DUMP>), static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const int tiles = ((M + QBM - 1) / QBM) * (N / QBN);
   const int grid = tiles < num_sms() ? tiles : num_sms();

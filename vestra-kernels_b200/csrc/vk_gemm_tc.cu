@@ -429,7 +429,8 @@ template <int MODE, bool PAIR>
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om, const GemmEpi& epi, int M, int N,
                    int K, int* err, cudaStream_t s) {
   using C = Cfg<MODE, PAIR>;
-  static int max_units = 0;  // CTAs (or CTA pairs) that can be resident at once
+  // CTAs (or CTA pairs) that can be resident at once, per device
+  int& max_units = *per_device_slot(reinterpret_cast<const void*>(k_gemm_bf16<MODE, PAIR>));
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(GEMM_THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
@@ -451,8 +452,7 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& 
   cfg.attrs = attr;
   cfg.numAttrs = na;
   if (max_units == 0) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_bf16<MODE, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(C::SMEM));
+    cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(k_gemm_bf16<MODE, PAIR>), static_cast<int>(C::SMEM));
     if (e != cudaSuccess) return e;
     int n = 0;
     if (PAIR) {

@@ -55,6 +55,12 @@ bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
 int num_sms();
 // Launch attributes for programmatic dependent launch (off with VK_NO_PDL).
 bool pdl_enabled();
+// Raises `func`'s dynamic shared-memory limit to `bytes` on the current
+// device (once per device and function; the attribute is per device).
+cudaError_t ensure_smem_limit(const void* func, int bytes);
+// Per-device cache slot for launch facts computed once (e.g. resident CTA
+// pairs); returns a pointer to an int initialised to 0 for (key, device).
+int* per_device_slot(const void* key);
 
 // bf16 x bf16 -> f32 tcgen05 GEMM: C[M,N] = A[M,K] . W[N,K]^T (both K-major),
 // K % 64 == 0, N % 128 == 0.  Returns a cudaError_t.

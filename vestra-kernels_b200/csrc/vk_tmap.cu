@@ -1,3 +1,7 @@
+#include <map>
+#include <mutex>
+#include <set>
+#include <tuple>
 #include <stdlib.h>
 // vk_tmap.cu -- host helpers shared by the TMA kernels: tensor-map encoding
 // (driver entry point fetched through the runtime, no libcuda link) and the
@@ -51,18 +55,41 @@ bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
   return r == CUDA_SUCCESS;
 }
 
+cudaError_t ensure_smem_limit(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int>> done;  // (function, device, bytes)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(func, dev, bytes);
+  if (done.count(key)) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert(key);
+  return e;
+}
+
+int* per_device_slot(const void* key) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> slots;  // std::map nodes never move
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  return &slots[std::make_pair(key, dev)];
+}
+
 bool pdl_enabled() {
   static const bool on = getenv("VK_NO_PDL") == nullptr;
   return on;
 }
 
-int num_sms() {
-  static int n = 0;
+int num_sms() {  // of the current device
+  int& n = *per_device_slot(reinterpret_cast<const void*>(&num_sms));
   if (n == 0) {
-    int dev = 0;
+    int dev = 0, v = 0;
     cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n = v > 0 ? v : 148;
   }
   return n;
 }
