@@ -1,7 +1,5 @@
 #include <map>
 #include <mutex>
-#include <set>
-#include <tuple>
 #include <stdlib.h>
 // vk_tmap.cu -- host helpers shared by the TMA kernels: tensor-map encoding
 // (driver entry point fetched through the runtime, no libcuda link) and the
@@ -57,15 +55,15 @@ bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
 
 cudaError_t ensure_smem_limit(const void* func, int bytes) {
   static std::mutex mu;
-  static std::set<std::tuple<const void*, int, int>> done;  // (function, device, bytes)
+  static std::map<std::pair<const void*, int>, int> limit;  // (function, device) -> largest limit set
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lock(mu);
-  const auto key = std::make_tuple(func, dev, bytes);
-  if (done.count(key)) return cudaSuccess;
+  int& cur = limit[std::make_pair(func, dev)];
+  if (bytes <= cur) return cudaSuccess;  // only ever raised: smaller launches fit under it
   e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) done.insert(key);
+  if (e == cudaSuccess) cur = bytes;
   return e;
 }
 
