@@ -59,7 +59,8 @@ typedef struct {
  * (src/cuda.rs:383-443). */
 int vk_init(int device, vk_ctx** out);
 int vk_destroy(vk_ctx* ctx);
-/* Use this cudaStream_t (NULL = legacy default stream) for later calls. */
+/* Use this cudaStream_t for later calls (NULL = the context's own stream,
+ * a non-blocking stream created by vk_init). */
 int vk_stream_set(vk_ctx* ctx, void* stream);
 /* Arithmetic of the f32-interface operators below (default VK_MATH_F32). */
 int vk_set_math(vk_ctx* ctx, int math);

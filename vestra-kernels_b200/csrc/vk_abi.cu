@@ -70,6 +70,8 @@ extern "C" int vk_init(int device, vk_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_err, sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
   if (e != cudaSuccess) {
+    if (ctx->d_err) cudaFree(ctx->d_err);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return vk_cuda_status(e, "vk_init");
   }
