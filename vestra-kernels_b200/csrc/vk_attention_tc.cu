@@ -54,7 +54,7 @@ constexpr size_t ATT_SMEM = 1024 + TILE_BYTES * (4 + 2 * AST) + 512;
 template <int OUT>
 __global__ void __launch_bounds__(A_THREADS, 1)
     k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, int heads, int tokens, int items, void* out,
+                   const __grid_constant__ CUtensorMap tmV, int heads, int tokens, int items, int tpi, void* out,
                    __half* out_q8d, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -73,12 +73,14 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pairs = (tokens + 2 * AQ - 1) / (2 * AQ);  // query-tile pairs per (image, head)
+  // An item is `tpi` (2, or 1 when pairs would leave SMs idle) query tiles
+  // of one (image, head).
+  const int pairs = (tokens + tpi * AQ - 1) / (tpi * AQ);  // items per (image, head)
   const int nb = (tokens + AKV - 1) / AKV;
   auto item_tiles = [&](int it, int& bh, int& q0) {
     bh = it / pairs;
-    q0 = (it - bh * pairs) * 2 * AQ;
-    return (tokens - q0 > AQ) ? 2 : 1;  // tile 1 may not exist
+    q0 = (it - bh * pairs) * tpi * AQ;
+    return (tpi == 2 && tokens - q0 > AQ) ? 2 : 1;  // tile 1 may not exist
   };
 
   if (threadIdx.x == 0) {
@@ -362,7 +364,10 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
                                int heads, int tokens, void* out, __half* q8d, int* err, cudaStream_t s) {
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(k_attention_tc<OUT>), static_cast<int>(ATT_SMEM));
   if (e != cudaSuccess) return e;
-  const int items = ((tokens + 2 * AQ - 1) / (2 * AQ)) * images * heads;
+  // tile pairs share each K/V block; single tiles when pairs would not fill the SMs
+  int tpi = 2;
+  if (((tokens + 2 * AQ - 1) / (2 * AQ)) * images * heads < num_sms()) tpi = 1;
+  const int items = ((tokens + tpi * AQ - 1) / (tpi * AQ)) * images * heads;
   const int grid = items < num_sms() ? items : num_sms();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -374,7 +379,7 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
   la[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = la;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_attention_tc<OUT>, mq, mk, mv, heads, tokens, items, out, q8d, err);
+  return cudaLaunchKernelEx(&cfg, k_attention_tc<OUT>, mq, mk, mv, heads, tokens, items, tpi, out, q8d, err);
 }
 
 cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int images,
