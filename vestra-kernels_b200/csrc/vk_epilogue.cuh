@@ -155,7 +155,7 @@ __device__ __forceinline__ void epi_direct(const GemmEpi& p, int row, int col0, 
 
 template <int MODE>
 __device__ __forceinline__ void epilogue_chunk(const GemmEpi& p, int row, int col0, int N, float (&v)[32]) {
-  epi_math<MODE>(p, row, col0, v, p.bias ? p.bias + col0 : nullptr, p.scale ? p.scale + col0 : nullptr);
+  epi_math<MODE, true>(p, row, col0, v, p.bias ? p.bias + col0 : nullptr, p.scale ? p.scale + col0 : nullptr);
   epi_direct<MODE>(p, row, col0, N, v);
 }
 
