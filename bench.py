@@ -221,6 +221,77 @@ def patch_embed_ms(vk, ctx, B, gh, gw, steps, math):
     return e0.elapsed_time(e1) / steps
 
 
+# representative DPT-head consumer shapes at 336 x 504 (grid 24 x 36): the
+# encoder output to CHW, a 3x3 fusion convolution on the 4x-upsampled map,
+# the align-corners 2x resize, and the final resize + UV add + 3x3 head
+# convolution fused (src/conv.rs:304)
+DPT_FUSION = (128, 128, 96, 144)
+DPT_RESIZE = (128, 96, 144, 192, 288)
+DPT_FINAL = (64, 32, 192, 288, 336, 504)
+FP32_SIMT_NOMINAL = 148 * 128 * 2 * 1.965e9 / 1e12  # TFLOP/s at the maximum SM clock (nominal, not measured)
+
+
+def dpt_consumers(vk, ctx, B, gh, gw, reps=5):
+    """CUDA-event ms per call over B images of the DPT head's consumers of the
+    encoder output (random-init filters, N(0,1) maps), each with its roofline."""
+    import torch
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    r = np.random.default_rng(5)
+    peaks = load_peaks()
+    res = {}
+    n = gh * gw
+    tm = torch.randn(B * n * E, device="cuda")
+    chw = torch.empty_like(tm)
+    ms = timed(lambda: vk.token_to_chw_batched(tm, B, n, E, chw, ctx=ctx))
+    gbs = 2 * tm.numel() * 4 / ms / 1e6
+    res["token_to_chw"] = {"ms": round(ms, 4), "gbs": gbs, "frac_of_hbm": gbs / peaks["hbm_gbs"]}
+    del tm, chw
+    ci, co, h, w = DPT_FUSION
+    f = vk.WinogradF2Filter(ctx, (r.standard_normal(co * ci * 9) * 0.05).astype(np.float32), ci, co)
+    x = torch.randn(B * ci * h * w, device="cuda")
+    y = torch.empty(B * co * h * w, device="cuda")
+    bias = torch.zeros(co, device="cuda")
+    ms = timed(lambda: vk.conv3x3_batched(x, B, h, w, f, bias, y, ctx=ctx))
+    wino = 2.0 * 16 * ci * co * ((h + 1) // 2) * ((w + 1) // 2) * B / (ms / 1e3) / 1e12
+    res["conv3x3_%dx%d_%dx%d" % (ci, co, h, w)] = {
+        "ms": round(ms, 4), "winograd_tflops": wino, "frac_of_fp32_simt": wino / FP32_SIMT_NOMINAL,
+        "direct_equiv_tflops": 2.0 * 9 * ci * co * h * w * B / (ms / 1e3) / 1e12}
+    del x, y
+    c, ih, iw, oh, ow = DPT_RESIZE
+    x = torch.randn(B * c * ih * iw, device="cuda")
+    y = torch.empty(B * c * oh * ow, device="cuda")
+    ms = timed(lambda: vk.bilinear_resize_align_corners(x, B * c, ih, iw, oh, ow, y, ctx=ctx))
+    gbs = (x.numel() + y.numel()) * 4 / ms / 1e6
+    res["resize_ac_%dx%d_to_%dx%d" % (ih, iw, oh, ow)] = {"ms": round(ms, 4), "gbs": gbs,
+                                                         "frac_of_hbm": gbs / peaks["hbm_gbs"]}
+    del x, y
+    ci, co, ih, iw, oh, ow = DPT_FINAL
+    f = vk.WinogradF2Filter(ctx, (r.standard_normal(co * ci * 9) * 0.05).astype(np.float32), ci, co)
+    x = torch.randn(B * ci * ih * iw, device="cuda")
+    add = torch.randn(ci * oh * ow, device="cuda")
+    y = torch.empty(B * co * oh * ow, device="cuda")
+    bias = torch.zeros(co, device="cuda")
+    ms = timed(lambda: vk.conv3x3_batched(x, B, ih, iw, f, bias, y, resize_to=(oh, ow), add=add, ctx=ctx))
+    wino = 2.0 * 16 * ci * co * ((oh + 1) // 2) * ((ow + 1) // 2) * B / (ms / 1e3) / 1e12
+    res["resize_ac_conv3x3_%dx%d_to_%dx%d" % (ci, co, oh, ow)] = {
+        "ms": round(ms, 4), "winograd_tflops": wino, "frac_of_fp32_simt": wino / FP32_SIMT_NOMINAL}
+    res["note"] = ("f32, outside `value`; conv roofline against the nominal fp32 SIMT peak "
+                   "%.1f TFLOP/s (148 SMs x 128 lanes x 2 x 1965 MHz), resize/transpose against measured HBM"
+                   % FP32_SIMT_NOMINAL)
+    return res
+
+
 def run_vestra(args, rank, world, local_rank):
     import torch
 
@@ -235,6 +306,11 @@ def run_vestra(args, rank, world, local_rank):
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)  # a real stream: the encoder is graph-captured on it
     ctx = vk.Context(local_rank, stream=stream)
+    if args.dpt_only:
+        if rank == 0:
+            print(json.dumps({"dpt_consumers": dpt_consumers(vk, ctx, B, gh, gw, reps=args.steps), "images": B}),
+                  flush=True)
+        return
     enc = vk.Encoder(ctx, make_layers(0), math=math)
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     x = torch.randn(B, T, E, device="cuda", generator=g)
@@ -288,6 +364,8 @@ def run_vestra(args, rank, world, local_rank):
     # the step before the encoder: patch embedding of the same batch (images
     # [B, 3, 14 gh, 14 gw] -> tokens), timed on its own
     pe_ms = patch_embed_ms(vk, ctx, B, gh, gw, args.steps, math)
+    # the step after it: the DPT head's consumers of the encoder output
+    dpt = dpt_consumers(vk, ctx, B, gh, gw) if not args.no_dpt else None
 
     ms, e2e_ms = max_over_ranks(ms), max_over_ranks(e2e_ms)
     if rank != 0:
@@ -337,6 +415,7 @@ def run_vestra(args, rank, world, local_rank):
             "ms_per_step": round(pe_ms, 4), "images_per_s": B / (pe_ms / 1e3),
             "tflops": 2.0 * B * gh * gw * 588 * E / (pe_ms / 1e3) / 1e12,
             "note": "patchify + 588->768 projection + cls/position assembly of the same batch, outside `value`"},
+        "dpt_consumers": dpt,
     }
     if world == 1 and not args.no_cpu:
         s = cpu_reference_seconds_per_image(gh, gw, make_layers(0), reps=1)
@@ -355,6 +434,9 @@ def main():
     ap.add_argument("--images", type=int, default=64)
     ap.add_argument("--grid", default="24x36")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-dpt", action="store_true", help="skip the DPT-consumer timings")
+    ap.add_argument("--dpt-only", action="store_true",
+                    help="run only the DPT-consumer kernels on --images images (for profiling)")
     args = ap.parse_args()
     args.grid = tuple(int(v) for v in args.grid.split("x"))
     args.warmup = max(args.warmup, 3)

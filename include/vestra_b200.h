@@ -258,6 +258,59 @@ int vk_encoder_profile(vk_ctx* ctx, vk_encoder* enc, size_t images, size_t grid_
 int vk_encoder_last_launches(const vk_encoder* enc);
 int vk_encoder_release(vk_encoder* enc);
 
+/* ------------------------------------------------- DPT head consumers
+ * The step after the encoder: token-major features to CHW maps, bilinear
+ * resizes and the 3x3 convolutions of the DPT head, all f32 on device
+ * buffers, batch 1 as the reference (plus batched conveniences). */
+
+/* src/cuda.rs:278-291 vestra_token_to_chw_f32 / CudaRuntime::token_to_chw_f32
+ * (src/cuda.rs:1032-1068): token_major [tokens, channels] -> chw [channels,
+ * tokens].  tokens or channels == 0 is VK_ERR_INVALID_ARGUMENT, as the
+ * reference's CudaError::LengthMismatch. */
+int vk_token_to_chw_f32(vk_ctx* ctx, const float* token_major, size_t tokens, size_t channels, float* chw);
+/* `images` [tokens, channels] matrices back to back -> `images` CHW maps. */
+int vk_token_to_chw_f32_batched(vk_ctx* ctx, const float* token_major, size_t images, size_t tokens,
+                                size_t channels, float* chw);
+/* src/resample.rs:10-78 bilinear_resize (half-pixel centres, clamp to edge):
+ * input [c, ih, iw] -> out [c, oh, ow].  Any zero size is a no-op, as the
+ * reference's early return.  Bit-exact with the reference's f32 arithmetic. */
+int vk_bilinear_resize_f32(vk_ctx* ctx, const float* input, size_t c, size_t ih, size_t iw, size_t oh, size_t ow,
+                           float* out);
+/* src/resample.rs:184-249 bilinear_resize_align_corners; as above. */
+int vk_bilinear_resize_align_corners_f32(vk_ctx* ctx, const float* input, size_t c, size_t ih, size_t iw, size_t oh,
+                                         size_t ow, float* out);
+
+/* A prepared 3x3 convolution filter: WinogradF2Filter
+ * (prepare_winograd_f2_filter, src/conv.rs:175-178; the transform of
+ * src/conv.rs:136-160) held on the device as U [16][in_c][out_c]. */
+typedef struct vk_conv3x3 vk_conv3x3;
+/* weight_host: OIHW [out_c, in_c, 3, 3] f32. */
+int vk_conv3x3_prepare(vk_ctx* ctx, const float* weight_host, size_t in_c, size_t out_c, vk_conv3x3** out);
+/* conv3x3_winograd_f2_prepared / _prepared_relu_input (src/conv.rs:282-302,
+ * 667-679): stride 1, pad 1, input [in_c, ih, iw] -> out [out_c, ih, iw];
+ * bias [out_c] or NULL (device); relu_input != 0 applies max(x, 0) to every
+ * input sample.  in_c / out_c must match the filter (VK_ERR_INVALID_ARGUMENT).
+ * The transforms follow the reference's F(2x2, 3x3) arithmetic; the
+ * transform-domain sums run over ascending in_c with fused multiply-adds. */
+int vk_conv3x3_forward(vk_ctx* ctx, const vk_conv3x3* conv, const float* input, size_t in_c, size_t ih, size_t iw,
+                       size_t out_c, const float* bias, int relu_input, float* out);
+/* conv3x3_winograd_f2_prepared_resize_align_corners (src/conv.rs:304-484):
+ * input [in_c, ih, iw] resized (align corners) to [in_c, oh, ow], plus `add`
+ * ([in_c, oh, ow] or NULL), then convolved -> out [out_c, oh, ow].  Equal
+ * bit for bit to vk_bilinear_resize_align_corners_f32, the add, and
+ * vk_conv3x3_forward in sequence. */
+int vk_conv3x3_resize_ac_forward(vk_ctx* ctx, const vk_conv3x3* conv, const float* input, size_t in_c, size_t ih,
+                                 size_t iw, size_t oh, size_t ow, const float* add, size_t out_c, const float* bias,
+                                 float* out);
+/* Batched forms: `images` inputs / outputs back to back; `add` is shared by
+ * all images (the DPT UV embedding depends on the size only). */
+int vk_conv3x3_forward_batched(vk_ctx* ctx, const vk_conv3x3* conv, size_t images, const float* input, size_t ih,
+                               size_t iw, const float* bias, int relu_input, float* out);
+int vk_conv3x3_resize_ac_forward_batched(vk_ctx* ctx, const vk_conv3x3* conv, size_t images, const float* input,
+                                         size_t ih, size_t iw, size_t oh, size_t ow, const float* add,
+                                         const float* bias, float* out);
+int vk_conv3x3_release(vk_conv3x3* conv);
+
 #ifdef __cplusplus
 }
 #endif

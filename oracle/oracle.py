@@ -265,6 +265,74 @@ def prepend_cls_add_pos(patches, cls, position, patch_count, embed) -> np.ndarra
     return out
 
 
+# ---- DPT head consumers (the step after the encoder)
+
+def token_to_chw(token_major, tokens, channels) -> np.ndarray:
+    """vestra_token_to_chw_f32 (src/cuda.rs:278-291): [tokens, channels] -> [channels, tokens]."""
+    out = np.empty((channels, tokens), np.float32)
+    lib().vko_token_to_chw(_p(_f32(token_major)), _sz(tokens), _sz(channels), _p(out))
+    return out
+
+
+def bilinear_resize(x, oh, ow, align_corners=False) -> np.ndarray:
+    """bilinear_resize / bilinear_resize_align_corners (src/resample.rs:10-99, 151-249); x [c, ih, iw]."""
+    x = _f32(x)
+    c, ih, iw = x.shape
+    out = np.zeros((c, oh, ow), np.float32)
+    fn = lib().vko_bilinear_resize_align_corners if align_corners else lib().vko_bilinear_resize
+    fn(_p(x), _sz(c), _sz(ih), _sz(iw), _sz(oh), _sz(ow), _p(out))
+    return out
+
+
+def winograd_f2_filter(weight, in_c, out_c) -> np.ndarray:
+    """transformed_winograd_filter (src/conv.rs:121-171): OIHW -> U [16, in_c, out_c]."""
+    u = np.empty((16, in_c, out_c), np.float32)
+    lib().vko_winograd_f2_filter(_p(_f32(weight)), _sz(in_c), _sz(out_c), _p(u))
+    return u
+
+
+def conv3x3_winograd_f2(x, weight, bias=None, relu_input=False) -> np.ndarray:
+    """conv3x3_winograd_f2 / _relu_input (src/conv.rs:266-280, 651-831); x [in_c, h, w], OIHW weight."""
+    x = _f32(x)
+    in_c, h, w = x.shape
+    out_c = np.shape(weight)[0]
+    u = winograd_f2_filter(weight, in_c, out_c)
+    out = np.empty((out_c, h, w), np.float32)
+    b = _f32(bias) if bias is not None else None
+    lib().vko_conv3x3_winograd_f2(_p(x), _sz(in_c), _sz(h), _sz(w), _p(u), _sz(out_c),
+                                  _p(b) if b is not None else None, ctypes.c_int(int(relu_input)), _p(out))
+    return out
+
+
+def conv3x3_winograd_f2_resize_ac(x, oh, ow, add, weight, bias=None) -> np.ndarray:
+    """conv3x3_winograd_f2_prepared_resize_align_corners (src/conv.rs:304-484)."""
+    x = _f32(x)
+    in_c, ih, iw = x.shape
+    out_c = np.shape(weight)[0]
+    u = winograd_f2_filter(weight, in_c, out_c)
+    out = np.empty((out_c, oh, ow), np.float32)
+    a = _f32(add) if add is not None else None
+    b = _f32(bias) if bias is not None else None
+    lib().vko_conv3x3_winograd_f2_resize_ac(_p(x), _sz(in_c), _sz(ih), _sz(iw), _sz(oh), _sz(ow),
+                                            _p(a) if a is not None else None, _p(u), _sz(out_c),
+                                            _p(b) if b is not None else None, _p(out))
+    return out
+
+
+def conv2d_naive(x, weight, stride=1, pad=1, bias=None) -> np.ndarray:
+    """conv2d_naive (src/conv.rs:950-1000): direct convolution, OIHW weight."""
+    x = _f32(x)
+    weight = _f32(weight)
+    in_c, ih, iw = x.shape
+    out_c, _, kh, kw = weight.shape
+    oh, ow = (ih + 2 * pad - kh) // stride + 1, (iw + 2 * pad - kw) // stride + 1
+    out = np.empty((out_c, oh, ow), np.float32)
+    b = _f32(bias) if bias is not None else None
+    lib().vko_conv2d_naive(_p(x), _sz(in_c), _sz(ih), _sz(iw), _p(weight), _sz(out_c), _sz(kh), _sz(kw),
+                           _sz(stride), _sz(pad), _p(b) if b is not None else None, _p(out))
+    return out
+
+
 LAYER_KEYS = ["ln1_g", "ln1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ls1",
               "ln2_g", "ln2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "ls2"]
 # optional Q/K LayerNorm vectors of a layer dict -> struct fields

@@ -600,3 +600,242 @@ void vko_encoder_layer(float* x, size_t tokens, size_t grid_h, size_t grid_w, si
   free(wqkv); free(wo); free(w1); free(w2);
   free(h); free(q); free(k); free(v); free(att); free(tok); free(o); free(f); free(pos);
 }
+
+/* ------------------------------------------------ DPT head consumers */
+
+/* src/cuda.rs:278-291 vestra_token_to_chw_f32 */
+void vko_token_to_chw(const float* token_major, size_t tokens, size_t channels, float* chw) {
+  for (size_t t = 0; t < tokens; ++t)
+    for (size_t c = 0; c < channels; ++c) chw[c * tokens + t] = token_major[t * channels + c];
+}
+
+/* src/resample.rs:82-99 src_coord (half-pixel centres) */
+static void hp_coord(size_t dst, float scale, size_t len_in, size_t* i0, size_t* i1, float* frac) {
+  const float src = ((float)dst + 0.5f) * scale - 0.5f;
+  const float sc = src > 0.0f ? src : 0.0f;
+  size_t a = (size_t)floorf(sc);
+  const size_t last = len_in > 0 ? len_in - 1 : 0;
+  if (a > last) a = last;
+  size_t b = a + 1 > last ? last : a + 1;
+  float f = b == a ? 0.0f : sc - (float)a;
+  f = f < 0.0f ? 0.0f : (f > 1.0f ? 1.0f : f);
+  *i0 = a;
+  *i1 = b;
+  *frac = f;
+}
+
+/* src/resample.rs:151-167 src_coord_align_corners (and the identical
+ * closure of src/conv.rs:320-336) */
+static void ac_coord(size_t dst, size_t len_in, size_t len_out, size_t* i0, size_t* i1, float* frac) {
+  if (len_in <= 1) {
+    *i0 = 0;
+    *i1 = 0;
+    *frac = 0.0f;
+    return;
+  }
+  float src = len_out <= 1 ? 0.0f : (float)dst * (float)(len_in - 1) / (float)(len_out - 1);
+  const float hi = (float)(len_in - 1);
+  src = src < 0.0f ? 0.0f : (src > hi ? hi : src);
+  size_t a = (size_t)floorf(src);
+  if (a > len_in - 1) a = len_in - 1;
+  const size_t b = a + 1 > len_in - 1 ? len_in - 1 : a + 1;
+  float f = b == a ? 0.0f : src - (float)a;
+  f = f < 0.0f ? 0.0f : (f > 1.0f ? 1.0f : f);
+  *i0 = a;
+  *i1 = b;
+  *frac = f;
+}
+
+/* the blend of src/resample.rs:66-71 / 240-245 */
+static float blend(const float* plane, size_t iw, size_t y0, size_t y1, float fy, size_t x0, size_t x1, float fx) {
+  const float top = plane[y0 * iw + x0] * (1.0f - fx) + plane[y0 * iw + x1] * fx;
+  const float bot = plane[y1 * iw + x0] * (1.0f - fx) + plane[y1 * iw + x1] * fx;
+  return top * (1.0f - fy) + bot * fy;
+}
+
+/* src/resample.rs:10-78 */
+void vko_bilinear_resize(const float* input, size_t c, size_t ih, size_t iw, size_t oh, size_t ow, float* out) {
+  if (ih == 0 || iw == 0 || oh == 0 || ow == 0) return;
+  const float sy = (float)ih / (float)oh, sx = (float)iw / (float)ow;
+  for (size_t ch = 0; ch < c; ++ch)
+    for (size_t y = 0; y < oh; ++y) {
+      size_t y0, y1;
+      float fy;
+      hp_coord(y, sy, ih, &y0, &y1, &fy);
+      for (size_t x = 0; x < ow; ++x) {
+        size_t x0, x1;
+        float fx;
+        hp_coord(x, sx, iw, &x0, &x1, &fx);
+        out[(ch * oh + y) * ow + x] = blend(input + ch * ih * iw, iw, y0, y1, fy, x0, x1, fx);
+      }
+    }
+}
+
+/* src/resample.rs:184-249 */
+void vko_bilinear_resize_align_corners(const float* input, size_t c, size_t ih, size_t iw, size_t oh, size_t ow,
+                                       float* out) {
+  if (ih == 0 || iw == 0 || oh == 0 || ow == 0) return;
+  for (size_t ch = 0; ch < c; ++ch)
+    for (size_t y = 0; y < oh; ++y) {
+      size_t y0, y1;
+      float fy;
+      ac_coord(y, ih, oh, &y0, &y1, &fy);
+      for (size_t x = 0; x < ow; ++x) {
+        size_t x0, x1;
+        float fx;
+        ac_coord(x, iw, ow, &x0, &x1, &fx);
+        out[(ch * oh + y) * ow + x] = blend(input + ch * ih * iw, iw, y0, y1, fy, x0, x1, fx);
+      }
+    }
+}
+
+/* src/conv.rs:136-160: U = G g G^T per (oc, ic), stored [position][ic][oc] */
+void vko_winograd_f2_filter(const float* weight, size_t in_c, size_t out_c, float* u) {
+  for (size_t oc = 0; oc < out_c; ++oc)
+    for (size_t ic = 0; ic < in_c; ++ic) {
+      const float* g = weight + (oc * in_c + ic) * 9;
+      float t[4][3], uu[16];
+      for (int j = 0; j < 3; ++j) {
+        const float a = g[j], b = g[3 + j], c = g[6 + j];
+        t[0][j] = a;
+        t[1][j] = 0.5f * (a + b + c);
+        t[2][j] = 0.5f * (a - b + c);
+        t[3][j] = c;
+      }
+      for (int i = 0; i < 4; ++i) {
+        const float a = t[i][0], b = t[i][1], c = t[i][2];
+        uu[i * 4] = a;
+        uu[i * 4 + 1] = 0.5f * (a + b + c);
+        uu[i * 4 + 2] = 0.5f * (a - b + c);
+        uu[i * 4 + 3] = c;
+      }
+      for (int p = 0; p < 16; ++p) u[(p * in_c + ic) * out_c + oc] = uu[p];
+    }
+}
+
+/* The input transform B^T d B of one 4x4 patch (src/conv.rs:382-405). */
+static void winograd_input_tf(const float d[16], float v[16]) {
+  float col[16];
+  for (int j = 0; j < 4; ++j) {
+    const float a = d[j], b = d[4 + j], c = d[8 + j], e = d[12 + j];
+    col[j] = a - c;
+    col[4 + j] = b + c;
+    col[8 + j] = c - b;
+    col[12 + j] = b - e;
+  }
+  for (int i = 0; i < 4; ++i) {
+    const float a = col[i * 4], b = col[i * 4 + 1], c = col[i * 4 + 2], e = col[i * 4 + 3];
+    v[i * 4] = a - c;
+    v[i * 4 + 1] = b + c;
+    v[i * 4 + 2] = c - b;
+    v[i * 4 + 3] = b - e;
+  }
+}
+
+/* The transform-domain products and the output transform A^T M A of one
+ * tile for every oc (src/conv.rs:407-481): v [16][in_c] of the tile. */
+static void winograd_tile_out(const float* v, const float* u, size_t in_c, size_t out_c, const float* bias,
+                              size_t ty, size_t tx, size_t oh, size_t ow, float* out) {
+  for (size_t oc = 0; oc < out_c; ++oc) {
+    float m[16];
+    for (int p = 0; p < 16; ++p) {
+      float sum = 0.0f;
+      for (size_t ic = 0; ic < in_c; ++ic) sum += u[(p * in_c + ic) * out_c + oc] * v[p * in_c + ic];
+      m[p] = sum;
+    }
+    float q[8];
+    for (int j = 0; j < 4; ++j) {
+      q[j] = m[j] + m[4 + j] + m[8 + j];
+      q[4 + j] = m[4 + j] - m[8 + j] - m[12 + j];
+    }
+    const float b = bias ? bias[oc] : 0.0f;
+    const float val[4] = {q[0] + q[1] + q[2] + b, q[1] - q[2] - q[3] + b, q[4] + q[5] + q[6] + b,
+                          q[5] - q[6] - q[7] + b};
+    for (size_t dy = 0; dy < 2; ++dy)
+      for (size_t dx = 0; dx < 2; ++dx) {
+        const size_t y = ty * 2 + dy, x = tx * 2 + dx;
+        if (y < oh && x < ow) out[(oc * oh + y) * ow + x] = val[dy * 2 + dx];
+      }
+  }
+}
+
+/* src/conv.rs:681-831 */
+void vko_conv3x3_winograd_f2(const float* input, size_t in_c, size_t ih, size_t iw, const float* u, size_t out_c,
+                             const float* bias, int relu_input, float* out) {
+  const size_t tiles_y = (ih + 1) / 2, tiles_x = (iw + 1) / 2;
+#pragma omp parallel for schedule(dynamic, 4)
+  for (size_t tile = 0; tile < tiles_y * tiles_x; ++tile) {
+    const size_t ty = tile / tiles_x, tx = tile % tiles_x;
+    float* v = (float*)malloc(sizeof(float) * 16 * in_c);
+    for (size_t ic = 0; ic < in_c; ++ic) {
+      float d[16], t[16];
+      for (int dy = 0; dy < 4; ++dy)
+        for (int dx = 0; dx < 4; ++dx) {
+          const long sy = (long)(ty * 2) + dy - 1, sx = (long)(tx * 2) + dx - 1;
+          float s = (sy >= 0 && sy < (long)ih && sx >= 0 && sx < (long)iw) ? input[(ic * ih + sy) * iw + sx] : 0.0f;
+          d[dy * 4 + dx] = relu_input ? (s > 0.0f ? s : 0.0f) : s;
+        }
+      winograd_input_tf(d, t);
+      for (int p = 0; p < 16; ++p) v[p * in_c + ic] = t[p];
+    }
+    winograd_tile_out(v, u, in_c, out_c, bias, ty, tx, ih, iw, out);
+    free(v);
+  }
+}
+
+/* src/conv.rs:304-484 */
+void vko_conv3x3_winograd_f2_resize_ac(const float* input, size_t in_c, size_t ih, size_t iw, size_t oh, size_t ow,
+                                       const float* add, const float* u, size_t out_c, const float* bias, float* out) {
+  const size_t tiles_y = (oh + 1) / 2, tiles_x = (ow + 1) / 2;
+#pragma omp parallel for schedule(dynamic, 4)
+  for (size_t tile = 0; tile < tiles_y * tiles_x; ++tile) {
+    const size_t ty = tile / tiles_x, tx = tile % tiles_x;
+    float* v = (float*)malloc(sizeof(float) * 16 * in_c);
+    for (size_t ic = 0; ic < in_c; ++ic) {
+      float d[16], t[16];
+      for (int dy = 0; dy < 4; ++dy)
+        for (int dx = 0; dx < 4; ++dx) {
+          const long y = (long)(ty * 2) + dy - 1, x = (long)(tx * 2) + dx - 1;
+          float s = 0.0f;
+          if (y >= 0 && y < (long)oh && x >= 0 && x < (long)ow) {
+            size_t y0, y1, x0, x1;
+            float fy, fx;
+            ac_coord((size_t)y, ih, oh, &y0, &y1, &fy);
+            ac_coord((size_t)x, iw, ow, &x0, &x1, &fx);
+            const float* plane = input + ic * ih * iw;
+            const float top = plane[y0 * iw + x0] * (1.0f - fx) + plane[y0 * iw + x1] * fx;
+            const float bot = plane[y1 * iw + x0] * (1.0f - fx) + plane[y1 * iw + x1] * fx;
+            s = top * (1.0f - fy) + bot * fy + (add ? add[(ic * oh + y) * ow + x] : 0.0f);
+          }
+          d[dy * 4 + dx] = s;
+        }
+      winograd_input_tf(d, t);
+      for (int p = 0; p < 16; ++p) v[p * in_c + ic] = t[p];
+    }
+    winograd_tile_out(v, u, in_c, out_c, bias, ty, tx, oh, ow, out);
+    free(v);
+  }
+}
+
+/* src/conv.rs:950-1000 */
+void vko_conv2d_naive(const float* input, size_t in_c, size_t ih, size_t iw, const float* weight, size_t out_c,
+                      size_t kh, size_t kw, size_t stride, size_t pad, const float* bias, float* out) {
+  const size_t oh = (ih + 2 * pad - kh) / stride + 1, ow = (iw + 2 * pad - kw) / stride + 1;
+  for (size_t oc = 0; oc < out_c; ++oc)
+    for (size_t y = 0; y < oh; ++y)
+      for (size_t x = 0; x < ow; ++x) {
+        float acc = 0.0f;
+        for (size_t ic = 0; ic < in_c; ++ic)
+          for (size_t ky = 0; ky < kh; ++ky) {
+            const long iy = (long)(y * stride + ky) - (long)pad;
+            if (iy < 0 || iy >= (long)ih) continue;
+            for (size_t kx = 0; kx < kw; ++kx) {
+              const long ix = (long)(x * stride + kx) - (long)pad;
+              if (ix < 0 || ix >= (long)iw) continue;
+              acc += input[(ic * ih + iy) * iw + ix] * weight[((oc * in_c + ic) * kh + ky) * kw + kx];
+            }
+          }
+        if (bias) acc += bias[oc];
+        out[(oc * oh + y) * ow + x] = acc;
+      }
+}

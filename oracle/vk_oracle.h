@@ -131,6 +131,34 @@ int vko_patchify_nchw(const float* image, size_t height, size_t width, size_t pa
 void vko_prepend_cls_add_pos(const float* patches, const float* cls, const float* position, size_t patch_count,
                              size_t embed, float* tokens);
 
+/* ---- DPT head consumers: the step after the encoder ---- */
+/* src/cuda.rs:278-291 vestra_token_to_chw_f32: token-major [tokens,
+ * channels] -> CHW [channels, tokens]. */
+void vko_token_to_chw(const float* token_major, size_t tokens, size_t channels, float* chw);
+/* src/resample.rs:10-99 bilinear_resize: half-pixel centres, clamp to edge;
+ * input [c, ih, iw] -> out [c, oh, ow]; any zero size leaves out untouched. */
+void vko_bilinear_resize(const float* input, size_t c, size_t ih, size_t iw, size_t oh, size_t ow, float* out);
+/* src/resample.rs:151-249 bilinear_resize_align_corners. */
+void vko_bilinear_resize_align_corners(const float* input, size_t c, size_t ih, size_t iw, size_t oh, size_t ow,
+                                       float* out);
+/* src/conv.rs:121-171 transformed_winograd_filter: OIHW [out_c, in_c, 3, 3]
+ * -> U [16][in_c][out_c] (F(2x2, 3x3), G g G^T). */
+void vko_winograd_f2_filter(const float* weight, size_t in_c, size_t out_c, float* u);
+/* src/conv.rs:681-831 conv3x3_winograd_f2_impl: stride 1, pad 1, output
+ * [out_c, ih, iw]; relu_input applies max(x, 0) to every loaded sample;
+ * bias may be NULL.  The transform-domain sums run over ascending ic with
+ * separately rounded products, as the scalar fallback. */
+void vko_conv3x3_winograd_f2(const float* input, size_t in_c, size_t ih, size_t iw, const float* u, size_t out_c,
+                             const float* bias, int relu_input, float* out);
+/* src/conv.rs:304-484 conv3x3_winograd_f2_prepared_resize_align_corners: the
+ * input is resized (align corners) to [in_c, oh, ow], plus `add` (NULL or
+ * [in_c, oh, ow]), then convolved; output [out_c, oh, ow]. */
+void vko_conv3x3_winograd_f2_resize_ac(const float* input, size_t in_c, size_t ih, size_t iw, size_t oh, size_t ow,
+                                       const float* add, const float* u, size_t out_c, const float* bias, float* out);
+/* src/conv.rs:950-1000 conv2d_naive: direct convolution, OIHW weights. */
+void vko_conv2d_naive(const float* input, size_t in_c, size_t ih, size_t iw, const float* weight, size_t out_c,
+                      size_t kh, size_t kw, size_t stride, size_t pad, const float* bias, float* out);
+
 /* Threads used by the parallel loops (rows are independent and each keeps
  * the scalar reduction order, so results do not depend on this). */
 void vko_set_threads(int n);

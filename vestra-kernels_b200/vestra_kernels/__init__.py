@@ -81,6 +81,16 @@ SIGNATURES = {
     "vk_patch_embed_prepare": (_I, [_P, _S, _S, _S, _P, _P, _P, _I, ctypes.POINTER(_P)]),
     "vk_patch_embed_forward": (_I, [_P, _P, _S, _S, _S, _P, _P, _P]),
     "vk_patch_embed_release": (_I, [_P]),
+    "vk_token_to_chw_f32": (_I, [_P, _P, _S, _S, _P]),
+    "vk_token_to_chw_f32_batched": (_I, [_P, _P, _S, _S, _S, _P]),
+    "vk_bilinear_resize_f32": (_I, [_P, _P, _S, _S, _S, _S, _S, _P]),
+    "vk_bilinear_resize_align_corners_f32": (_I, [_P, _P, _S, _S, _S, _S, _S, _P]),
+    "vk_conv3x3_prepare": (_I, [_P, _P, _S, _S, ctypes.POINTER(_P)]),
+    "vk_conv3x3_forward": (_I, [_P, _P, _P, _S, _S, _S, _S, _P, _I, _P]),
+    "vk_conv3x3_resize_ac_forward": (_I, [_P, _P, _P, _S, _S, _S, _S, _S, _P, _S, _P, _P]),
+    "vk_conv3x3_forward_batched": (_I, [_P, _P, _S, _P, _S, _S, _P, _I, _P]),
+    "vk_conv3x3_resize_ac_forward_batched": (_I, [_P, _P, _S, _P, _S, _S, _S, _S, _P, _P, _P]),
+    "vk_conv3x3_release": (_I, [_P]),
 }
 
 _lib = None
@@ -389,6 +399,91 @@ class PatchEmbed:
                 self.handle = None
         except Exception:
             pass
+
+
+# ---------------------------------------------------------------- DPT head consumers
+
+def token_to_chw_f32(token_major, tokens: int, channels: int, chw, ctx: Context | None = None) -> None:
+    """CudaRuntime::token_to_chw_f32 (src/cuda.rs:1032-1068): [tokens, channels] -> [channels, tokens];
+    zero sizes raise, as the reference's LengthMismatch."""
+    ctx = ctx or default_context()
+    _check(lib().vk_token_to_chw_f32(ctx.handle, _ptr(token_major), tokens, channels, _ptr(chw)))
+
+
+def token_to_chw_batched(token_major, images: int, tokens: int, channels: int, chw,
+                         ctx: Context | None = None) -> None:
+    """`images` token-major matrices back to back -> `images` CHW maps."""
+    ctx = ctx or default_context()
+    _check(lib().vk_token_to_chw_f32_batched(ctx.handle, _ptr(token_major), images, tokens, channels, _ptr(chw)))
+
+
+def bilinear_resize(x, c: int, ih: int, iw: int, oh: int, ow: int, out, ctx: Context | None = None) -> None:
+    """resample::bilinear_resize (src/resample.rs:10): half-pixel centres, clamp to edge."""
+    ctx = ctx or default_context()
+    _check(lib().vk_bilinear_resize_f32(ctx.handle, _ptr(x), c, ih, iw, oh, ow, _ptr(out)))
+
+
+def bilinear_resize_align_corners(x, c: int, ih: int, iw: int, oh: int, ow: int, out,
+                                  ctx: Context | None = None) -> None:
+    """resample::bilinear_resize_align_corners (src/resample.rs:184)."""
+    ctx = ctx or default_context()
+    _check(lib().vk_bilinear_resize_align_corners_f32(ctx.handle, _ptr(x), c, ih, iw, oh, ow, _ptr(out)))
+
+
+class WinogradF2Filter:
+    """prepare_winograd_f2_filter (src/conv.rs:175): an OIHW [out_c, in_c, 3, 3]
+    filter transformed once to U [16, in_c, out_c] on the device."""
+
+    def __init__(self, ctx: Context, weight, in_c: int, out_c: int):
+        import numpy as np
+
+        w = np.ascontiguousarray(weight, dtype=np.float32)
+        if w.size != out_c * in_c * 9:
+            raise ValueError(f"weight has {w.size} values, expected out_c * in_c * 9 = {out_c * in_c * 9}")
+        h = ctypes.c_void_p()
+        st = _check(lib().vk_conv3x3_prepare(ctx.handle, w.ctypes.data_as(ctypes.c_void_p), in_c, out_c,
+                                             ctypes.byref(h)))
+        if st != VK_OK:
+            raise VestraError(st, last_error())
+        self.handle, self.ctx, self.in_c, self.out_c = h, ctx, in_c, out_c
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib().vk_conv3x3_release(self.handle)
+                self.handle = None
+        except Exception:
+            pass
+
+
+def conv3x3_winograd_f2_prepared(x, in_c: int, ih: int, iw: int, filt: WinogradF2Filter, out_c: int, bias, out,
+                                 relu_input: bool = False, ctx: Context | None = None) -> None:
+    """conv3x3_winograd_f2_prepared / _prepared_relu_input (src/conv.rs:282, 667): stride 1, pad 1."""
+    ctx = ctx or filt.ctx
+    _check(lib().vk_conv3x3_forward(ctx.handle, filt.handle, _ptr(x), in_c, ih, iw, out_c, _ptr(bias),
+                                    int(relu_input), _ptr(out)))
+
+
+def conv3x3_winograd_f2_prepared_resize_align_corners(x, in_c: int, ih: int, iw: int, oh: int, ow: int, add,
+                                                      filt: WinogradF2Filter, out_c: int, bias, out,
+                                                      ctx: Context | None = None) -> None:
+    """conv3x3_winograd_f2_prepared_resize_align_corners (src/conv.rs:304): resize + add fused into the conv."""
+    ctx = ctx or filt.ctx
+    _check(lib().vk_conv3x3_resize_ac_forward(ctx.handle, filt.handle, _ptr(x), in_c, ih, iw, oh, ow, _ptr(add),
+                                              out_c, _ptr(bias), _ptr(out)))
+
+
+def conv3x3_batched(x, images: int, ih: int, iw: int, filt: WinogradF2Filter, bias, out, relu_input: bool = False,
+                    resize_to=None, add=None, ctx: Context | None = None) -> None:
+    """`images` convolutions back to back; resize_to=(oh, ow) fuses the align-corners resize (+ shared add)."""
+    ctx = ctx or filt.ctx
+    if resize_to is None:
+        _check(lib().vk_conv3x3_forward_batched(ctx.handle, filt.handle, images, _ptr(x), ih, iw, _ptr(bias),
+                                                int(relu_input), _ptr(out)))
+    else:
+        oh, ow = resize_to
+        _check(lib().vk_conv3x3_resize_ac_forward_batched(ctx.handle, filt.handle, images, _ptr(x), ih, iw, oh, ow,
+                                                          _ptr(add), _ptr(bias), _ptr(out)))
 
 
 class _LayerWeights(ctypes.Structure):
