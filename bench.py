@@ -231,7 +231,7 @@ DPT_FINAL = (64, 32, 192, 288, 336, 504)
 FP32_SIMT_NOMINAL = 148 * 128 * 2 * 1.965e9 / 1e12  # TFLOP/s at the maximum SM clock (nominal, not measured)
 
 
-def dpt_consumers(vk, ctx, B, gh, gw, reps=5):
+def dpt_consumers(vk, ctx, B, gh, gw, reps=5, math=None):
     """CUDA-event ms per call over B images of the DPT head's consumers of the
     encoder output (random-init filters, N(0,1) maps), each with its roofline."""
     import torch
@@ -258,7 +258,8 @@ def dpt_consumers(vk, ctx, B, gh, gw, reps=5):
     res["token_to_chw"] = {"ms": round(ms, 4), "gbs": gbs, "frac_of_hbm": gbs / peaks["hbm_gbs"]}
     del tm, chw
     ci, co, h, w = DPT_FUSION
-    f = vk.WinogradF2Filter(ctx, (r.standard_normal(co * ci * 9) * 0.05).astype(np.float32), ci, co)
+    cmath = vk.MATH_BF16 if math is None else math  # the tensor-core products; f32 for the reference's arithmetic
+    f = vk.WinogradF2Filter(ctx, (r.standard_normal(co * ci * 9) * 0.05).astype(np.float32), ci, co, math=cmath)
     x = torch.randn(B * ci * h * w, device="cuda")
     y = torch.empty(B * co * h * w, device="cuda")
     bias = torch.zeros(co, device="cuda")
@@ -277,7 +278,7 @@ def dpt_consumers(vk, ctx, B, gh, gw, reps=5):
                                                          "frac_of_hbm": gbs / peaks["hbm_gbs"]}
     del x, y
     ci, co, ih, iw, oh, ow = DPT_FINAL
-    f = vk.WinogradF2Filter(ctx, (r.standard_normal(co * ci * 9) * 0.05).astype(np.float32), ci, co)
+    f = vk.WinogradF2Filter(ctx, (r.standard_normal(co * ci * 9) * 0.05).astype(np.float32), ci, co, math=cmath)
     x = torch.randn(B * ci * ih * iw, device="cuda")
     add = torch.randn(ci * oh * ow, device="cuda")
     y = torch.empty(B * co * oh * ow, device="cuda")

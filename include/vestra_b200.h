@@ -286,6 +286,13 @@ int vk_bilinear_resize_align_corners_f32(vk_ctx* ctx, const float* input, size_t
 typedef struct vk_conv3x3 vk_conv3x3;
 /* weight_host: OIHW [out_c, in_c, 3, 3] f32. */
 int vk_conv3x3_prepare(vk_ctx* ctx, const float* weight_host, size_t in_c, size_t out_c, vk_conv3x3** out);
+/* As vk_conv3x3_prepare with a math mode: VK_MATH_F32 (the SIMT kernel
+ * above) or VK_MATH_BF16 -- the 16 transform-domain products on the tensor
+ * cores with V and U rounded to bf16 and f32 accumulation (1e-2 relative
+ * L2 bar, the precision class of the encoder's bf16 math); the transforms
+ * and the resize stay f32. */
+int vk_conv3x3_prepare_math(vk_ctx* ctx, const float* weight_host, size_t in_c, size_t out_c, int math,
+                            vk_conv3x3** out);
 /* conv3x3_winograd_f2_prepared / _prepared_relu_input (src/conv.rs:282-302,
  * 667-679): stride 1, pad 1, input [in_c, ih, iw] -> out [out_c, ih, iw];
  * bias [out_c] or NULL (device); relu_input != 0 applies max(x, 0) to every
@@ -298,7 +305,8 @@ int vk_conv3x3_forward(vk_ctx* ctx, const vk_conv3x3* conv, const float* input, 
  * input [in_c, ih, iw] resized (align corners) to [in_c, oh, ow], plus `add`
  * ([in_c, oh, ow] or NULL), then convolved -> out [out_c, oh, ow].  Equal
  * bit for bit to vk_bilinear_resize_align_corners_f32, the add, and
- * vk_conv3x3_forward in sequence. */
+ * vk_conv3x3_forward in sequence (which is how it runs: the resized map,
+ * images * in_c * oh * ow floats, lives in the context's workspace). */
 int vk_conv3x3_resize_ac_forward(vk_ctx* ctx, const vk_conv3x3* conv, const float* input, size_t in_c, size_t ih,
                                  size_t iw, size_t oh, size_t ow, const float* add, size_t out_c, const float* bias,
                                  float* out);

@@ -215,3 +215,38 @@ def test_token_to_chw_batched(vk, ctx, oracle_lib):
     got = host(out).reshape(n, channels, tokens)
     for i in range(n):
         np.testing.assert_array_equal(got[i], oracle_lib.token_to_chw(x[i], tokens, channels))
+
+
+# bf16 math: the 16 transform-domain products on the tensor cores (V and U
+# rounded to bf16, f32 accumulation).  Bar: 1e-2 relative L2 against the f32
+# oracle, the precision class of the encoder's bf16 math.
+BF16_BAR = 1e-2
+
+
+@pytest.mark.parametrize("in_c,out_c,h,w", [(3, 5, 7, 9), (16, 16, 11, 9), (20, 40, 13, 6), (128, 128, 48, 72),
+                                            (64, 32, 96, 144), (33, 7, 2, 65), (1, 1, 1, 1), (48, 96, 33, 130)])
+def test_conv3x3_bf16_matches_oracle(vk, ctx, oracle_lib, in_c, out_c, h, w):
+    x, wt, b = conv_inputs(in_c * 7 + w, in_c, out_c, h, w, "normal")
+    f = vk.WinogradF2Filter(ctx, wt, in_c, out_c, math=vk.MATH_BF16)
+    out = torch.empty(out_c * h * w, device="cuda")
+    vk.conv3x3_winograd_f2_prepared(dev(x), in_c, h, w, f, out_c, dev(b), out, ctx=ctx)
+    assert rel_l2(host(out).reshape(out_c, h, w), oracle_lib.conv3x3_winograd_f2(x, wt, b)) <= BF16_BAR
+
+
+def test_conv3x3_bf16_relu_fused_and_batched(vk, ctx, oracle_lib):
+    in_c, out_c, ih, iw, oh, ow, n = 24, 40, 17, 23, 30, 41, 3
+    r = np.random.default_rng(11)
+    x = r.standard_normal((n, in_c, ih, iw)).astype(np.float32)
+    add = r.standard_normal((in_c, oh, ow)).astype(np.float32)
+    wt = (r.standard_normal((out_c, in_c, 3, 3)) * 0.05).astype(np.float32)
+    b = (r.standard_normal(out_c) * 0.1).astype(np.float32)
+    f = vk.WinogradF2Filter(ctx, wt, in_c, out_c, math=vk.MATH_BF16)
+    relu = torch.empty(n * out_c * ih * iw, device="cuda")
+    vk.conv3x3_batched(dev(x), n, ih, iw, f, dev(b), relu, relu_input=True, ctx=ctx)
+    fused = torch.empty(n * out_c * oh * ow, device="cuda")
+    vk.conv3x3_batched(dev(x), n, ih, iw, f, dev(b), fused, resize_to=(oh, ow), add=dev(add), ctx=ctx)
+    relu_h = host(relu).reshape(n, out_c, ih, iw)
+    fused_h = host(fused).reshape(n, out_c, oh, ow)
+    for i in range(n):
+        assert rel_l2(relu_h[i], oracle_lib.conv3x3_winograd_f2(x[i], wt, b, relu_input=True)) <= BF16_BAR
+        assert rel_l2(fused_h[i], oracle_lib.conv3x3_winograd_f2_resize_ac(x[i], oh, ow, add, wt, b)) <= BF16_BAR

@@ -13,14 +13,16 @@
 // operations in its order (explicit round-to-nearest intrinsics, so nothing
 // is contracted into an FMA): bit-exact.
 //
-// The convolution is one fused kernel per (32 tiles of 2x2 outputs, 32
-// output channels).  Per 16-channel slice it builds the transformed input
-// V = B^T d B of its tiles in shared memory (sampling through the fused
-// align-corners resize and add, or ReLU, where asked), stages the matching
-// slice of the prepared filter U, and accumulates the 16 transform-domain
-// products M_p = V_p U_p in registers: each thread owns one of the 16
-// positions for 8 tiles x 8 channels.  The output transform A^T M A then
-// runs from shared memory and writes the 2x2 outputs with the bias.
+// The convolution (f32 math) is one kernel per (4 x 8 tiles of 2x2 outputs,
+// 32 output channels).  Per 16-channel slice it builds the transformed input
+// V = B^T d B of its tiles in shared memory (ReLU on the samples where
+// asked), stages the matching slice of the prepared filter U, and
+// accumulates the 16 transform-domain products M_p = V_p U_p in registers:
+// each thread owns one of the 16 positions for 8 tiles x 8 channels.  The
+// output transform A^T M A then runs from shared memory and writes the 2x2
+// outputs with the bias.  bf16 math runs the products on the tensor cores
+// (k_conv3x3_wino_tc below).  The resize-fused form resizes (and adds) into
+// the context workspace with the resize kernel, then convolves.
 #include "vestra_b200.h"
 #include "vk_abi_internal.h"
 #include "vk_common.cuh"
@@ -30,8 +32,10 @@ using namespace vk;
 
 struct vk_conv3x3 {
   int device = 0;
+  int math = VK_MATH_F32;
   size_t in_c = 0, out_c = 0;
-  float* u = nullptr;  // [16][in_c][out_c]
+  float* u = nullptr;           // f32 math: [16][in_c][out_c]
+  __nv_bfloat16* ub = nullptr;  // bf16 math: [out_c / 32][in_c / 16][16][32 x 16 core-matrix tile]
 };
 
 namespace {
@@ -109,7 +113,8 @@ __device__ __forceinline__ float blend(const float* __restrict__ plane, int iw, 
 constexpr int RS_CH = 8, RS_X = 64;
 template <bool AC>
 __global__ void __launch_bounds__(RS_X) k_bilinear(const float* __restrict__ in, float* __restrict__ out, int c,
-                                                   int ih, int iw, int oh, int ow) {
+                                                   int ih, int iw, int oh, int ow, const float* __restrict__ add,
+                                                   int add_c) {
   const int x = blockIdx.x * RS_X + threadIdx.x, y = blockIdx.y;
   const int c0 = blockIdx.z * RS_CH;
   if (x >= ow) return;
@@ -118,8 +123,11 @@ __global__ void __launch_bounds__(RS_X) k_bilinear(const float* __restrict__ in,
 #pragma unroll
   for (int k = 0; k < RS_CH; ++k) {
     const int ch = c0 + k;
-    if (ch < c)
-      out[(static_cast<size_t>(ch) * oh + y) * ow + x] = blend(in + static_cast<size_t>(ch) * ih * iw, iw, cy, cx);
+    if (ch < c) {
+      float v = blend(in + static_cast<size_t>(ch) * ih * iw, iw, cy, cx);
+      if (add) v = __fadd_rn(v, __ldg(add + (static_cast<size_t>(ch % add_c) * oh + y) * ow + x));  // shared per image
+      out[(static_cast<size_t>(ch) * oh + y) * ow + x] = v;
+    }
   }
 }
 
@@ -163,13 +171,9 @@ constexpr int PU = KC * CO + 4;        // likewise for U
 constexpr int PM = CT * (CO + 1);      // per position plane of the products
 constexpr int CONV_THREADS = 256;      // 16 positions x (4 tile groups x 4 channel groups)
 constexpr int TBY = 4, TBX = 8;        // the CTA's tiles: 4 rows x 8 columns (CT)
-constexpr int PR = 2 * TBY + 2, PC = 2 * TBX + 2;  // its input patch: 10 x 18 samples per channel
-constexpr int A_FLOATS = 16 * PM > 16 * (PV + PU) ? 16 * PM : 16 * (PV + PU);
-enum { CONV_PLAIN = 0, CONV_RELU = 1, CONV_RESIZE_AC = 2 };
-template <int MODE>
-constexpr size_t conv_smem() {  // the resized patch and its coordinates only where the resize is fused
-  return sizeof(float) * A_FLOATS + (MODE == CONV_RESIZE_AC ? sizeof(float) * KC * PR * PC + sizeof(int4) * (PR + PC) : 0);
-}
+constexpr int A_FLOATS = 16 * PM > 16 * (PV + PU) ? 16 * PM : 16 * (PV + PU);  // V + U slices, then M
+enum { CONV_PLAIN = 0, CONV_RELU = 1 };
+constexpr size_t CONV_SMEM = sizeof(float) * A_FLOATS;
 static_assert(TBY * TBX == CT, "tile block");
 
 
@@ -194,12 +198,10 @@ __device__ __forceinline__ void input_transform(const float (&d)[16], float (&v)
   }
 }
 
-// input [images][in_c][ih][iw]; out [images][out_c][oh][ow] (oh, ow = ih, iw
-// unless MODE is CONV_RESIZE_AC); add [in_c][oh][ow] or null; u
-// [16][in_c][out_c]; bias [out_c] or null.
+// input [images][in_c][h][w]; out [images][out_c][h][w]; u [16][in_c][out_c];
+// bias [out_c] or null.
 template <int MODE>
 __global__ void __launch_bounds__(CONV_THREADS) k_conv3x3_wino(const float* __restrict__ input,
-                                                               const float* __restrict__ add,
                                                                const float* __restrict__ u,
                                                                const float* __restrict__ bias, float* __restrict__ out,
                                                                int in_c, int ih, int iw, int oh, int ow, int out_c) {
@@ -207,8 +209,6 @@ __global__ void __launch_bounds__(CONV_THREADS) k_conv3x3_wino(const float* __re
   float* sV = reinterpret_cast<float*>(smem4);
   float* sU = sV + 16 * PV;
   float* sM = sV;                 // reused after the last slice
-  float* sIn = sV + A_FLOATS;     // [KC][PR][PC] input patch of the slice
-  int4* sCoord = reinterpret_cast<int4*>(sIn + KC * PR * PC);  // resize: rows [PR], then columns [PC]
   const int tid = threadIdx.x;
   const int tiles_x = (ow + 1) / 2, tiles_y = (oh + 1) / 2;
   const int nbx = (tiles_x + TBX - 1) / TBX;
@@ -216,16 +216,6 @@ __global__ void __launch_bounds__(CONV_THREADS) k_conv3x3_wino(const float* __re
   const int py0 = bty * 2 - 1, px0 = btx * 2 - 1;                            // patch origin (pad 1)
   const int oc0 = blockIdx.y * CO;
   const float* in_img = input + static_cast<size_t>(blockIdx.z) * in_c * ih * iw;
-  if constexpr (MODE == CONV_RESIZE_AC) {
-    // source coordinates of the patch's rows and columns (align corners)
-    if (tid < PR + PC) {
-      const bool row = tid < PR;
-      const int d = row ? py0 + tid : px0 + tid - PR;
-      const int lim = row ? oh : ow;
-      const Coord c = row ? ac_coord(min(max(d, 0), lim - 1), ih, oh) : ac_coord(min(max(d, 0), lim - 1), iw, ow);
-      sCoord[tid] = make_int4(c.i0, c.i1, __float_as_int(c.f), 0);
-    }
-  }
 
   // this thread's tile for the input transform (fixed across slices)
   const int tt = tid & (CT - 1);
@@ -243,51 +233,26 @@ __global__ void __launch_bounds__(CONV_THREADS) k_conv3x3_wino(const float* __re
 
   for (int ic0 = 0; ic0 < in_c; ic0 += KC) {
     __syncthreads();  // the previous slice has been consumed
-    if constexpr (MODE == CONV_RESIZE_AC) {
-      // the slice's resized patch, each sample computed once; zero padding
-#pragma unroll 4
-      for (int e = tid; e < KC * PR * PC; e += CONV_THREADS) {
-        const int icl = e / (PR * PC), r = (e / PC) % PR, c = e % PC;
-        const int ic = ic0 + icl, y = py0 + r, x = px0 + c;
-        float s = 0.0f;
-        if (ic < in_c && y >= 0 && y < oh && x >= 0 && x < ow) {
-          const int4 a = sCoord[r], b = sCoord[PR + c];
-          s = __fadd_rn(blend(in_img + static_cast<size_t>(ic) * ih * iw, iw, Coord{a.x, a.y, __int_as_float(a.z)},
-                              Coord{b.x, b.y, __int_as_float(b.z)}),
-                        add ? __ldg(add + (static_cast<size_t>(ic) * oh + y) * ow + x) : 0.0f);
-        }
-        sIn[e] = s;
-      }
-      __syncthreads();
-    }
     // V of (tile tt, channels ic0 + icl) for icl = tid / 32 + {0, 8}
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int icl = (tid >> 5) + h * 8, ic = ic0 + icl;
       float d[16];
-      if constexpr (MODE == CONV_RESIZE_AC) {
-        const float* src = sIn + icl * PR * PC + (2 * tyl) * PC + 2 * txl;
 #pragma unroll
-        for (int dy = 0; dy < 4; ++dy)
+      for (int k = 0; k < 16; ++k) d[k] = 0.0f;
+      if (ic < in_c) {
+        const float* plane = in_img + static_cast<size_t>(ic) * ih * iw;
 #pragma unroll
-          for (int dx = 0; dx < 4; ++dx) d[dy * 4 + dx] = src[dy * PC + dx];
-      } else {
+        for (int dy = 0; dy < 4; ++dy) {
+          const int y = oy0 + dy;
+          if (y < 0 || y >= oh) continue;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) d[k] = 0.0f;
-        if (ic < in_c) {
-          const float* plane = in_img + static_cast<size_t>(ic) * ih * iw;
-#pragma unroll
-          for (int dy = 0; dy < 4; ++dy) {
-            const int y = oy0 + dy;
-            if (y < 0 || y >= oh) continue;
-#pragma unroll
-            for (int dx = 0; dx < 4; ++dx) {
-              const int x = ox0 + dx;
-              if (x < 0 || x >= ow) continue;
-              float s = __ldg(plane + static_cast<size_t>(y) * iw + x);
-              if constexpr (MODE == CONV_RELU) s = fmaxf(s, 0.0f);
-              d[dy * 4 + dx] = s;
-            }
+          for (int dx = 0; dx < 4; ++dx) {
+            const int x = ox0 + dx;
+            if (x < 0 || x >= ow) continue;
+            float s = __ldg(plane + static_cast<size_t>(y) * iw + x);
+            if constexpr (MODE == CONV_RELU) s = fmaxf(s, 0.0f);
+            d[dy * 4 + dx] = s;
           }
         }
       }
@@ -363,6 +328,249 @@ constexpr size_t DIM_MAX = size_t(1) << 20;
 
 }  // namespace
 
+// ---------------------------------------------------------------- conv on the tensor cores (bf16 math)
+// The 16 position products M_p = V_p U_p run as tcgen05 MMAs: per CTA 128
+// tiles (M) x 32 output channels (N) x 16 positions, accumulated in TMEM
+// (16 x 32 = all 512 columns).  K runs over 16-channel slices: 256 worker
+// threads build the slice's V (bf16, core-matrix K-major layout) in shared
+// memory, while one thread streams the prepared bf16 U slices in with bulk
+// copies and issues the 16 MMAs of the previous slice.  The epilogue reads
+// each tile row's 16 positions from TMEM and applies A^T M A in registers.
+namespace {
+
+constexpr int TM = 128;                      // tiles per CTA (MMA M)
+constexpr int TN = 32;                       // output channels per CTA (MMA N)
+constexpr int TK = 16;                       // input channels per slice (MMA K)
+constexpr int TC_WORKERS = 256;              // transform / epilogue threads
+constexpr int TC_THREADS = TC_WORKERS + 32;  // + the MMA and copy warp
+constexpr int A_POS = TM * TK * 2;           // 4 KB: one position's V slice
+constexpr int B_POS = TN * TK * 2;           // 1 KB: one position's U slice
+constexpr int A_SLICE = 16 * A_POS, B_SLICE = 16 * B_POS;
+constexpr size_t TC_SMEM = 1024 + 2 * (A_SLICE + B_SLICE) + 128;
+
+// K-major operand without swizzle: core matrices of 8 rows x 16 bytes; the
+// two along K (a 16-element slice) are 128 bytes apart (LBO), 8-row groups
+// 256 bytes apart (SBO).  Row r, element k at (r/8)*256 + (k/8)*128 + (r%8)*16 + (k%8)*2.
+__device__ __forceinline__ uint64_t desc_kmajor_core(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(128u >> 4) << 16;  // LBO
+  d |= static_cast<uint64_t>(256u >> 4) << 32;  // SBO
+  d |= static_cast<uint64_t>(1u) << 46;         // sm_100 descriptor version; layout 0 = no swizzle
+  return d;
+}
+__host__ __device__ constexpr int core_offset(int r, int k) { return (r / 8) * 256 + (k / 8) * 128 + (r % 8) * 16 + (k % 8) * 2; }
+
+// plain bulk copy global -> shared (no tensor map, no multicast)
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// U f32 [16][in_c][out_c] -> bf16 [out_c / 32][slices][16 positions][32 x 16 core-matrix tile], zero-padded
+__global__ void k_pack_u_bf16(const float* __restrict__ u, __nv_bfloat16* __restrict__ ub, int in_c, int out_c,
+                              int slices, int ocb) {
+  const size_t total = static_cast<size_t>(ocb) * slices * 16 * TN * TK;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(i % TK), n = static_cast<int>((i / TK) % TN);
+    const int p = static_cast<int>((i / (TK * TN)) % 16);
+    const size_t sb = i / (TK * TN * 16);
+    const int s = static_cast<int>(sb % slices), b = static_cast<int>(sb / slices);
+    const int ic = s * TK + k, oc = b * TN + n;
+    const float v = (ic < in_c && oc < out_c) ? u[(static_cast<size_t>(p) * in_c + ic) * out_c + oc] : 0.0f;
+    ub[sb * (16 * TN * TK) + p * (TN * TK) + core_offset(n, k) / 2] = __float2bfloat16_rn(v);
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_conv3x3_wino_tc(const float* __restrict__ input, const __nv_bfloat16* __restrict__ ub, const float* __restrict__ bias, float* __restrict__ out,
+                      int in_c, int ih, int iw, int oh, int ow, int out_c, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;                   // [2][16][4 KB]
+  uint8_t* sB = smem + 2 * A_SLICE;     // [2][16][1 KB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + 2 * B_SLICE);
+  uint64_t* a_full = bars;              // [2] count TC_WORKERS
+  uint64_t* b_full = bars + 2;          // [2] U slice landed
+  uint64_t* ab_free = bars + 4;         // [2] the slice's MMAs finished
+  uint64_t* acc_done = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int slices = (in_c + TK - 1) / TK;
+  const int tiles_x = (ow + 1) / 2, tiles_y = (oh + 1) / 2;
+  const int ocb = blockIdx.y, oc0 = ocb * TN;
+  const float* in_img = input + static_cast<size_t>(blockIdx.z) * in_c * ih * iw;
+  const __nv_bfloat16* ub_blk = ub + static_cast<size_t>(ocb) * slices * (16 * TN * TK);
+
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&a_full[b], TC_WORKERS);
+      mbar_init(&b_full[b], 1);
+      mbar_init(&ab_free[b], 1);
+    }
+    mbar_init(acc_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == TC_WORKERS / 32) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == TC_WORKERS / 32) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(TM, TN);
+      auto load_u = [&](int s) {
+        mbar_arrive_expect_tx(&b_full[s & 1], B_SLICE);
+        bulk_load(sB + (s & 1) * B_SLICE, ub_blk + static_cast<size_t>(s) * (16 * TN * TK), B_SLICE, &b_full[s & 1]);
+      };
+      load_u(0);
+      if (slices > 1) load_u(1);
+      for (int s = 0; s < slices && ok; ++s) {
+        const int b = s & 1;
+        const uint32_t ph = (s >> 1) & 1;
+        if (!(ok = mbar_wait(&b_full[b], ph, err, VK_DEV_TIMEOUT_MMA))) break;
+        if (!(ok = mbar_wait(&a_full[b], ph, err, VK_DEV_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + b * A_SLICE), b0 = smem_u32(sB + b * B_SLICE);
+#pragma unroll
+        for (int p = 0; p < 16; ++p)
+          umma_f16(tmem + p * TN, desc_kmajor_core(a0 + p * A_POS), desc_kmajor_core(b0 + p * B_POS), idesc,
+                   s > 0 ? 1u : 0u);
+        umma_commit(&ab_free[b]);
+        if (s + 2 < slices) {
+          if (!(ok = mbar_wait(&ab_free[b], ph, err, VK_DEV_TIMEOUT_MMA))) break;  // this slice's MMAs read sB[b]
+          load_u(s + 2);
+        }
+      }
+      umma_commit(acc_done);
+    }
+  } else {
+    // ---- V slices: thread (tile row m, channel half kh); the CTA takes 128
+    // consecutive tiles in row-major order (rows of consecutive tiles load
+    // best straight from global memory; L1 serves the patches' overlap)
+    const int m = tid & (TM - 1), kh = tid >> 7;
+    const int lin_t = blockIdx.x * TM + m;
+    const bool lin_ok = lin_t < tiles_x * tiles_y;
+    const int lin_ty = lin_ok ? lin_t / tiles_x : 0, lin_tx = lin_ok ? lin_t % tiles_x : 0;
+    for (int s = 0; s < slices && ok; ++s) {
+      const int b = s & 1;
+      uint32_t packed[16][4];
+#pragma unroll
+      for (int pr = 0; pr < 4; ++pr) {  // channel pairs of this thread's 8
+        float v2[2][16];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int icl = kh * 8 + pr * 2 + e;
+          float d[16];
+          const int ic = s * TK + icl;
+          const int y0 = lin_ty * 2 - 1, x0 = lin_tx * 2 - 1;
+          const bool live = ic < in_c && lin_ok;
+          const float* plane = in_img + static_cast<size_t>(live ? ic : 0) * ih * iw;
+#pragma unroll
+          for (int dy = 0; dy < 4; ++dy)
+#pragma unroll
+            for (int dx = 0; dx < 4; ++dx) {
+              const int y = y0 + dy, x = x0 + dx;
+              float v = 0.0f;
+              if (live && y >= 0 && y < oh && x >= 0 && x < ow) {
+                v = __ldg(plane + static_cast<size_t>(y) * iw + x);
+                if constexpr (MODE == CONV_RELU) v = fmaxf(v, 0.0f);
+              }
+              d[dy * 4 + dx] = v;
+            }
+          input_transform(d, v2[e]);
+        }
+#pragma unroll
+        for (int p = 0; p < 16; ++p) packed[p][pr] = pack_bf16x2(v2[0][p], v2[1][p]);
+      }
+      // the slice's A buffer is free once the MMAs of slice s - 2 have finished
+      if (s >= 2 && !(ok = mbar_wait(&ab_free[b], ((s >> 1) - 1) & 1, err, VK_DEV_TIMEOUT_OTHER))) break;
+      uint8_t* a = sA + b * A_SLICE + core_offset(m, kh * 8);
+#pragma unroll
+      for (int p = 0; p < 16; ++p)
+        *reinterpret_cast<uint4*>(a + p * A_POS) = make_uint4(packed[p][0], packed[p][1], packed[p][2], packed[p][3]);
+      fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
+      mbar_arrive(&a_full[b]);
+    }
+    // ---- epilogue: warp w reads lanes (tiles) of quarter w % 4, channels [16 (w / 4), +16)
+    if (ok && (ok = mbar_wait(acc_done, 0, err, VK_DEV_TIMEOUT_EPILOGUE))) {
+      tc_fence_after();
+      const int q = warp & 3, chh = warp >> 2;
+      const int mt = q * 32 + lane;
+      const int lt = blockIdx.x * TM + mt;
+      const int ty = lt / tiles_x, tx = lt % tiles_x;
+      float acc[4][16];
+#pragma unroll
+      for (int o = 0; o < 4; ++o)
+#pragma unroll
+        for (int c = 0; c < 16; ++c) acc[o][c] = 0.0f;
+      constexpr float AT[2][4] = {{1.f, 1.f, 1.f, 0.f}, {0.f, 1.f, -1.f, -1.f}};
+#pragma unroll
+      for (int p = 0; p < 16; ++p) {
+        uint32_t r[16];
+        tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + p * TN + chh * 16, r);
+        tmem_wait_ld();
+        const int i = p >> 2, j = p & 3;
+#pragma unroll
+        for (int dy = 0; dy < 2; ++dy)
+#pragma unroll
+          for (int dx = 0; dx < 2; ++dx) {
+            const float cf = AT[dy][i] * AT[dx][j];
+            if (cf == 0.0f) continue;
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              acc[dy * 2 + dx][c] = cf > 0.0f ? acc[dy * 2 + dx][c] + __uint_as_float(r[c])
+                                              : acc[dy * 2 + dx][c] - __uint_as_float(r[c]);
+          }
+      }
+      if (ty < tiles_y && tx < tiles_x) {
+        const int ty0 = ty * 2, tx0 = tx * 2;
+        float* out_img = out + static_cast<size_t>(blockIdx.z) * out_c * oh * ow;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int oc = oc0 + chh * 16 + c;
+          if (oc >= out_c) break;
+          const float bb = bias ? __ldg(bias + oc) : 0.0f;
+          float* plane = out_img + static_cast<size_t>(oc) * oh * ow;
+#pragma unroll
+          for (int dy = 0; dy < 2; ++dy)
+#pragma unroll
+            for (int dx = 0; dx < 2; ++dx) {
+              const int y = ty0 + dy, x = tx0 + dx;
+              if (y < oh && x < ow) plane[static_cast<size_t>(y) * ow + x] = acc[dy * 2 + dx][c] + bb;
+            }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == TC_WORKERS / 32) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
 // ---------------------------------------------------------------- C ABI
 extern "C" int vk_token_to_chw_f32_batched(vk_ctx* ctx, const float* token_major, size_t images, size_t tokens,
                                            size_t channels, float* chw) {
@@ -385,6 +593,21 @@ extern "C" int vk_token_to_chw_f32(vk_ctx* ctx, const float* token_major, size_t
   return vk_token_to_chw_f32_batched(ctx, token_major, 1, tokens, channels, chw);
 }
 
+// input [c][ih][iw] -> out [c][oh][ow]; add [add_c][oh][ow] (added to plane ch at ch % add_c) or null
+static int resize_launch(vk_ctx* ctx, const float* input, size_t c, size_t ih, size_t iw, size_t oh, size_t ow,
+                         const float* add, size_t add_c, float* out, bool ac, const char* name) {
+  const dim3 grid(static_cast<unsigned>((ow + RS_X - 1) / RS_X), static_cast<unsigned>(oh),
+                  static_cast<unsigned>((c + RS_CH - 1) / RS_CH));
+  if (grid.y > 65535 || grid.z > 65535) return vk_fail(VK_UNSUPPORTED_SHAPE, "%s: oh or channels out of range", name);
+  if (ac)
+    k_bilinear<true><<<grid, RS_X, 0, ctx->stream>>>(input, out, (int)c, (int)ih, (int)iw, (int)oh, (int)ow, add,
+                                                     (int)(add_c ? add_c : 1));
+  else
+    k_bilinear<false><<<grid, RS_X, 0, ctx->stream>>>(input, out, (int)c, (int)ih, (int)iw, (int)oh, (int)ow, add,
+                                                      (int)(add_c ? add_c : 1));
+  return vk_cuda_status(cudaGetLastError(), name);
+}
+
 static int resize_impl(vk_ctx* ctx, const float* input, size_t c, size_t ih, size_t iw, size_t oh, size_t ow,
                        float* out, bool ac, const char* name) {
   if (!ctx) return vk_fail(VK_ERR_INVALID_ARGUMENT, "%s: NULL context", name);
@@ -393,14 +616,7 @@ static int resize_impl(vk_ctx* ctx, const float* input, size_t c, size_t ih, siz
   if (!input || !out) return vk_fail(VK_ERR_INVALID_ARGUMENT, "%s: NULL buffer", name);
   if (ih > DIM_MAX || iw > DIM_MAX || oh > DIM_MAX || ow > DIM_MAX || c > DIM_MAX)
     return vk_fail(VK_UNSUPPORTED_SHAPE, "%s: dimension above 2^20", name);
-  const dim3 grid(static_cast<unsigned>((ow + RS_X - 1) / RS_X), static_cast<unsigned>(oh),
-                  static_cast<unsigned>((c + RS_CH - 1) / RS_CH));
-  if (grid.y > 65535 || grid.z > 65535) return vk_fail(VK_UNSUPPORTED_SHAPE, "%s: oh or channels out of range", name);
-  if (ac)
-    k_bilinear<true><<<grid, RS_X, 0, ctx->stream>>>(input, out, (int)c, (int)ih, (int)iw, (int)oh, (int)ow);
-  else
-    k_bilinear<false><<<grid, RS_X, 0, ctx->stream>>>(input, out, (int)c, (int)ih, (int)iw, (int)oh, (int)ow);
-  return vk_cuda_status(cudaGetLastError(), name);
+  return resize_launch(ctx, input, c, ih, iw, oh, ow, nullptr, 0, out, ac, name);
 }
 
 extern "C" int vk_bilinear_resize_f32(vk_ctx* ctx, const float* input, size_t c, size_t ih, size_t iw, size_t oh,
@@ -413,8 +629,11 @@ extern "C" int vk_bilinear_resize_align_corners_f32(vk_ctx* ctx, const float* in
   return resize_impl(ctx, input, c, ih, iw, oh, ow, out, true, "vk_bilinear_resize_align_corners_f32");
 }
 
-extern "C" int vk_conv3x3_prepare(vk_ctx* ctx, const float* weight_host, size_t in_c, size_t out_c, vk_conv3x3** out) {
+extern "C" int vk_conv3x3_prepare_math(vk_ctx* ctx, const float* weight_host, size_t in_c, size_t out_c, int math,
+                                       vk_conv3x3** out) {
   if (!ctx) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_conv3x3_prepare: NULL context");
+  if (math != VK_MATH_F32 && math != VK_MATH_BF16)
+    return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_conv3x3_prepare: math must be f32 or bf16");
   cudaSetDevice(ctx->device);
   if (!weight_host || !out) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_conv3x3_prepare: NULL argument");
   *out = nullptr;
@@ -424,6 +643,7 @@ extern "C" int vk_conv3x3_prepare(vk_ctx* ctx, const float* weight_host, size_t 
   float* w = nullptr;
   vk_conv3x3* cv = new vk_conv3x3();
   cv->device = ctx->device;
+  cv->math = math;
   cv->in_c = in_c;
   cv->out_c = out_c;
   cudaError_t e = cudaMalloc(&w, wn * sizeof(float));
@@ -435,10 +655,25 @@ extern "C" int vk_conv3x3_prepare(vk_ctx* ctx, const float* weight_host, size_t 
                                                                                           (int)out_c);
     e = cudaGetLastError();
   }
+  if (e == cudaSuccess && math == VK_MATH_BF16) {
+    const int slices = static_cast<int>((in_c + TK - 1) / TK), ocb = static_cast<int>((out_c + TN - 1) / TN);
+    const size_t n = static_cast<size_t>(ocb) * slices * 16 * TN * TK;
+    e = cudaMalloc(&cv->ub, n * sizeof(__nv_bfloat16));
+    if (e == cudaSuccess) {
+      k_pack_u_bf16<<<static_cast<int>((n + DT_THREADS - 1) / DT_THREADS < 4096 ? (n + DT_THREADS - 1) / DT_THREADS : 4096),
+                      DT_THREADS, 0, ctx->stream>>>(cv->u, cv->ub, (int)in_c, (int)out_c, slices, ocb);
+      e = cudaGetLastError();
+    }
+  }
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (w) cudaFree(w);
+  if (e == cudaSuccess && cv->ub) {  // bf16 math keeps only the packed filter
+    cudaFree(cv->u);
+    cv->u = nullptr;
+  }
   if (e != cudaSuccess) {
     if (cv->u) cudaFree(cv->u);
+    if (cv->ub) cudaFree(cv->ub);
     delete cv;
     return vk_cuda_status(e, "vk_conv3x3_prepare");
   }
@@ -446,25 +681,40 @@ extern "C" int vk_conv3x3_prepare(vk_ctx* ctx, const float* weight_host, size_t 
   return VK_OK;
 }
 
+extern "C" int vk_conv3x3_prepare(vk_ctx* ctx, const float* weight_host, size_t in_c, size_t out_c, vk_conv3x3** out) {
+  return vk_conv3x3_prepare_math(ctx, weight_host, in_c, out_c, VK_MATH_F32, out);
+}
+
 extern "C" int vk_conv3x3_release(vk_conv3x3* conv) {
   if (!conv) return VK_OK;
   cudaSetDevice(conv->device);
   if (conv->u) cudaFree(conv->u);
+  if (conv->ub) cudaFree(conv->ub);
   delete conv;
   return VK_OK;
 }
 
 template <int MODE>
-static int conv_launch(vk_ctx* ctx, const vk_conv3x3* cv, size_t images, const float* input, size_t ih, size_t iw,
-                       size_t oh, size_t ow, const float* add, const float* bias, float* out, const char* name) {
-  const size_t blocks = ((oh + 1) / 2 + TBY - 1) / TBY * (((ow + 1) / 2 + TBX - 1) / TBX);
+static int conv_launch(vk_ctx* ctx, const vk_conv3x3* cv, size_t images, const float* input, size_t h, size_t w,
+                       const float* bias, float* out, const char* name) {
+  const size_t tiles = ((h + 1) / 2) * ((w + 1) / 2);
+  if (cv->math == VK_MATH_BF16) {
+    const void* fn = reinterpret_cast<const void*>(k_conv3x3_wino_tc<MODE>);
+    VK_TRY_CUDA(ensure_smem_limit(fn, static_cast<int>(TC_SMEM)), name);
+    const dim3 grid(static_cast<unsigned>((tiles + TM - 1) / TM), static_cast<unsigned>((cv->out_c + TN - 1) / TN),
+                    static_cast<unsigned>(images));
+    k_conv3x3_wino_tc<MODE><<<grid, TC_THREADS, TC_SMEM, ctx->stream>>>(input, cv->ub, bias, out, (int)cv->in_c,
+                                                                        (int)h, (int)w, (int)h, (int)w,
+                                                                        (int)cv->out_c, ctx->d_err);
+    return vk_cuda_status(cudaGetLastError(), name);
+  }
+  const size_t blocks = ((h + 1) / 2 + TBY - 1) / TBY * (((w + 1) / 2 + TBX - 1) / TBX);
   const void* fn = reinterpret_cast<const void*>(k_conv3x3_wino<MODE>);
-  VK_TRY_CUDA(ensure_smem_limit(fn, static_cast<int>(conv_smem<MODE>())), name);
+  VK_TRY_CUDA(ensure_smem_limit(fn, static_cast<int>(CONV_SMEM)), name);
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>((cv->out_c + CO - 1) / CO),
                   static_cast<unsigned>(images));
-  k_conv3x3_wino<MODE><<<grid, CONV_THREADS, conv_smem<MODE>(), ctx->stream>>>(input, add, cv->u, bias, out, (int)cv->in_c,
-                                                                       (int)ih, (int)iw, (int)oh, (int)ow,
-                                                                       (int)cv->out_c);
+  k_conv3x3_wino<MODE><<<grid, CONV_THREADS, CONV_SMEM, ctx->stream>>>(input, cv->u, bias, out, (int)cv->in_c, (int)h,
+                                                                       (int)w, (int)h, (int)w, (int)cv->out_c);
   return vk_cuda_status(cudaGetLastError(), name);
 }
 
@@ -485,8 +735,8 @@ extern "C" int vk_conv3x3_forward_batched(vk_ctx* ctx, const vk_conv3x3* conv, s
   const char* name = "vk_conv3x3_forward";
   VK_TRY(conv_check(ctx, conv, images, input, ih, iw, ih, iw, out, name));
   if (images == 0 || ih == 0 || iw == 0) return VK_OK;
-  return relu_input ? conv_launch<CONV_RELU>(ctx, conv, images, input, ih, iw, ih, iw, nullptr, bias, out, name)
-                    : conv_launch<CONV_PLAIN>(ctx, conv, images, input, ih, iw, ih, iw, nullptr, bias, out, name);
+  return relu_input ? conv_launch<CONV_RELU>(ctx, conv, images, input, ih, iw, bias, out, name)
+                    : conv_launch<CONV_PLAIN>(ctx, conv, images, input, ih, iw, bias, out, name);
 }
 
 extern "C" int vk_conv3x3_forward(vk_ctx* ctx, const vk_conv3x3* conv, const float* input, size_t in_c, size_t ih,
@@ -504,7 +754,16 @@ extern "C" int vk_conv3x3_resize_ac_forward_batched(vk_ctx* ctx, const vk_conv3x
   VK_TRY(conv_check(ctx, conv, images, input, ih, iw, oh, ow, out, name));
   if (images == 0 || oh == 0 || ow == 0) return VK_OK;
   if (ih == 0 || iw == 0) return vk_fail(VK_ERR_INVALID_ARGUMENT, "%s: empty input", name);
-  return conv_launch<CONV_RESIZE_AC>(ctx, conv, images, input, ih, iw, oh, ow, add, bias, out, name);
+  // The resized + added map goes through the context's workspace: a
+  // high-occupancy resize kernel and then the plain convolution beat
+  // resampling inside the convolution (whose few resident warps cannot hide
+  // the gathers).  Same operations in the same order as the reference's
+  // fused form, so the result is the one of resize, add, conv in sequence.
+  const size_t planes = images * conv->in_c;
+  VK_TRY(ctx_reserve(ctx, planes * oh * ow * sizeof(float)));
+  float* mid = static_cast<float*>(ctx->ws);
+  VK_TRY(resize_launch(ctx, input, planes, ih, iw, oh, ow, add, conv->in_c, mid, true, name));
+  return conv_launch<CONV_PLAIN>(ctx, conv, images, mid, oh, ow, bias, out, name);
 }
 
 extern "C" int vk_conv3x3_resize_ac_forward(vk_ctx* ctx, const vk_conv3x3* conv, const float* input, size_t in_c,

@@ -86,6 +86,7 @@ SIGNATURES = {
     "vk_bilinear_resize_f32": (_I, [_P, _P, _S, _S, _S, _S, _S, _P]),
     "vk_bilinear_resize_align_corners_f32": (_I, [_P, _P, _S, _S, _S, _S, _S, _P]),
     "vk_conv3x3_prepare": (_I, [_P, _P, _S, _S, ctypes.POINTER(_P)]),
+    "vk_conv3x3_prepare_math": (_I, [_P, _P, _S, _S, _I, ctypes.POINTER(_P)]),
     "vk_conv3x3_forward": (_I, [_P, _P, _P, _S, _S, _S, _S, _P, _I, _P]),
     "vk_conv3x3_resize_ac_forward": (_I, [_P, _P, _P, _S, _S, _S, _S, _S, _P, _S, _P, _P]),
     "vk_conv3x3_forward_batched": (_I, [_P, _P, _S, _P, _S, _S, _P, _I, _P]),
@@ -434,15 +435,16 @@ class WinogradF2Filter:
     """prepare_winograd_f2_filter (src/conv.rs:175): an OIHW [out_c, in_c, 3, 3]
     filter transformed once to U [16, in_c, out_c] on the device."""
 
-    def __init__(self, ctx: Context, weight, in_c: int, out_c: int):
+    def __init__(self, ctx: Context, weight, in_c: int, out_c: int, math: int = MATH_F32):
+        """math: MATH_F32 (SIMT, the reference's f32 arithmetic) or MATH_BF16 (tensor-core products)."""
         import numpy as np
 
         w = np.ascontiguousarray(weight, dtype=np.float32)
         if w.size != out_c * in_c * 9:
             raise ValueError(f"weight has {w.size} values, expected out_c * in_c * 9 = {out_c * in_c * 9}")
         h = ctypes.c_void_p()
-        st = _check(lib().vk_conv3x3_prepare(ctx.handle, w.ctypes.data_as(ctypes.c_void_p), in_c, out_c,
-                                             ctypes.byref(h)))
+        st = _check(lib().vk_conv3x3_prepare_math(ctx.handle, w.ctypes.data_as(ctypes.c_void_p), in_c, out_c, math,
+                                                  ctypes.byref(h)))
         if st != VK_OK:
             raise VestraError(st, last_error())
         self.handle, self.ctx, self.in_c, self.out_c = h, ctx, in_c, out_c
