@@ -231,7 +231,7 @@ DPT_FINAL = (64, 32, 192, 288, 336, 504)
 FP32_SIMT_NOMINAL = 148 * 128 * 2 * 1.965e9 / 1e12  # TFLOP/s at the maximum SM clock (nominal, not measured)
 
 
-def dpt_consumers(vk, ctx, B, gh, gw, reps=5, math=None):
+def dpt_consumers(vk, ctx, B, gh, gw, reps=5):
     """CUDA-event ms per call over B images of the DPT head's consumers of the
     encoder output (random-init filters, N(0,1) maps), each with its roofline."""
     import torch
@@ -258,16 +258,19 @@ def dpt_consumers(vk, ctx, B, gh, gw, reps=5, math=None):
     res["token_to_chw"] = {"ms": round(ms, 4), "gbs": gbs, "frac_of_hbm": gbs / peaks["hbm_gbs"]}
     del tm, chw
     ci, co, h, w = DPT_FUSION
-    cmath = vk.MATH_BF16 if math is None else math  # the tensor-core products; f32 for the reference's arithmetic
-    f = vk.WinogradF2Filter(ctx, (r.standard_normal(co * ci * 9) * 0.05).astype(np.float32), ci, co, math=cmath)
+    wt = (r.standard_normal(co * ci * 9) * 0.05).astype(np.float32)
     x = torch.randn(B * ci * h * w, device="cuda")
     y = torch.empty(B * co * h * w, device="cuda")
     bias = torch.zeros(co, device="cuda")
-    ms = timed(lambda: vk.conv3x3_batched(x, B, h, w, f, bias, y, ctx=ctx))
-    wino = 2.0 * 16 * ci * co * ((h + 1) // 2) * ((w + 1) // 2) * B / (ms / 1e3) / 1e12
-    res["conv3x3_%dx%d_%dx%d" % (ci, co, h, w)] = {
-        "ms": round(ms, 4), "winograd_tflops": wino, "frac_of_fp32_simt": wino / FP32_SIMT_NOMINAL,
-        "direct_equiv_tflops": 2.0 * 9 * ci * co * h * w * B / (ms / 1e3) / 1e12}
+    for mname, m in (("bf16", vk.MATH_BF16), ("f32", vk.MATH_F32)):
+        f = vk.WinogradF2Filter(ctx, wt, ci, co, math=m)
+        ms = timed(lambda: vk.conv3x3_batched(x, B, h, w, f, bias, y, ctx=ctx))
+        wino = 2.0 * 16 * ci * co * ((h + 1) // 2) * ((w + 1) // 2) * B / (ms / 1e3) / 1e12
+        res["conv3x3_%dx%d_%dx%d_%s" % (ci, co, h, w, mname)] = {
+            "ms": round(ms, 4), "winograd_tflops": wino,
+            "frac": wino / (peaks["bf16_sustained"] if m == vk.MATH_BF16 else FP32_SIMT_NOMINAL),
+            "of": "measured bf16 sustained (tensor)" if m == vk.MATH_BF16 else "nominal fp32 SIMT",
+            "direct_equiv_tflops": 2.0 * 9 * ci * co * h * w * B / (ms / 1e3) / 1e12}
     del x, y
     c, ih, iw, oh, ow = DPT_RESIZE
     x = torch.randn(B * c * ih * iw, device="cuda")
@@ -278,18 +281,20 @@ def dpt_consumers(vk, ctx, B, gh, gw, reps=5, math=None):
                                                          "frac_of_hbm": gbs / peaks["hbm_gbs"]}
     del x, y
     ci, co, ih, iw, oh, ow = DPT_FINAL
-    f = vk.WinogradF2Filter(ctx, (r.standard_normal(co * ci * 9) * 0.05).astype(np.float32), ci, co, math=cmath)
+    wt = (r.standard_normal(co * ci * 9) * 0.05).astype(np.float32)
     x = torch.randn(B * ci * ih * iw, device="cuda")
     add = torch.randn(ci * oh * ow, device="cuda")
     y = torch.empty(B * co * oh * ow, device="cuda")
     bias = torch.zeros(co, device="cuda")
-    ms = timed(lambda: vk.conv3x3_batched(x, B, ih, iw, f, bias, y, resize_to=(oh, ow), add=add, ctx=ctx))
-    wino = 2.0 * 16 * ci * co * ((oh + 1) // 2) * ((ow + 1) // 2) * B / (ms / 1e3) / 1e12
-    res["resize_ac_conv3x3_%dx%d_to_%dx%d" % (ci, co, oh, ow)] = {
-        "ms": round(ms, 4), "winograd_tflops": wino, "frac_of_fp32_simt": wino / FP32_SIMT_NOMINAL}
-    res["note"] = ("f32, outside `value`; conv roofline against the nominal fp32 SIMT peak "
-                   "%.1f TFLOP/s (148 SMs x 128 lanes x 2 x 1965 MHz), resize/transpose against measured HBM"
-                   % FP32_SIMT_NOMINAL)
+    for mname, m in (("bf16", vk.MATH_BF16), ("f32", vk.MATH_F32)):
+        f = vk.WinogradF2Filter(ctx, wt, ci, co, math=m)
+        ms = timed(lambda: vk.conv3x3_batched(x, B, ih, iw, f, bias, y, resize_to=(oh, ow), add=add, ctx=ctx))
+        res["resize_ac_conv3x3_%dx%d_to_%dx%d_%s" % (ci, co, oh, ow, mname)] = {
+            "ms": round(ms, 4),
+            "winograd_tflops": 2.0 * 16 * ci * co * ((oh + 1) // 2) * ((ow + 1) // 2) * B / (ms / 1e3) / 1e12}
+    res["note"] = ("outside `value`. Convolutions: bf16 math = tensor-core Winograd products (f32 transforms), "
+                   "f32 math = the reference's f32 arithmetic on the SIMT cores (nominal peak %.1f TFLOP/s: "
+                   "148 SMs x 128 lanes x 2 x 1965 MHz); resize / transpose against measured HBM" % FP32_SIMT_NOMINAL)
     return res
 
 

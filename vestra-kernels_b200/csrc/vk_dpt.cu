@@ -106,10 +106,10 @@ __device__ __forceinline__ float blend(const float* __restrict__ plane, int iw, 
   return __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, y.f));
 }
 
-// One CTA per (64 columns of an output row, 8 channels): the row's source
-// coordinate once, the thread's column once, then the channels' samples,
-// unrolled so that their gathers are in flight together (stores coalesce
-// along the row).
+// One CTA per (64 columns of an output row, 8 channels): the source
+// coordinates and the four neighbour offsets once per thread, then the
+// channels' samples by pointer increments (unrolled, so that several
+// channels' gathers are in flight together; stores coalesce along the row).
 constexpr int RS_CH = 8, RS_X = 64;
 template <bool AC>
 __global__ void __launch_bounds__(RS_X) k_bilinear(const float* __restrict__ in, float* __restrict__ out, int c,
@@ -120,14 +120,24 @@ __global__ void __launch_bounds__(RS_X) k_bilinear(const float* __restrict__ in,
   if (x >= ow) return;
   const Coord cy = AC ? ac_coord(y, ih, oh) : hp_coord(y, __fdiv_rn(static_cast<float>(ih), static_cast<float>(oh)), ih);
   const Coord cx = AC ? ac_coord(x, iw, ow) : hp_coord(x, __fdiv_rn(static_cast<float>(iw), static_cast<float>(ow)), iw);
+  const int o00 = cy.i0 * iw + cx.i0, o01 = cy.i0 * iw + cx.i1, o10 = cy.i1 * iw + cx.i0, o11 = cy.i1 * iw + cx.i1;
+  const float gx = __fsub_rn(1.0f, cx.f), gy = __fsub_rn(1.0f, cy.f);
+  const size_t in_plane = static_cast<size_t>(ih) * iw, out_plane = static_cast<size_t>(oh) * ow;
+  const float* src = in + c0 * in_plane;
+  float* dst = out + c0 * out_plane + static_cast<size_t>(y) * ow + x;
+  const int n = min(RS_CH, c - c0);
+  const int yx = y * ow + x;
 #pragma unroll
   for (int k = 0; k < RS_CH; ++k) {
-    const int ch = c0 + k;
-    if (ch < c) {
-      float v = blend(in + static_cast<size_t>(ch) * ih * iw, iw, cy, cx);
-      if (add) v = __fadd_rn(v, __ldg(add + (static_cast<size_t>(ch % add_c) * oh + y) * ow + x));  // shared per image
-      out[(static_cast<size_t>(ch) * oh + y) * ow + x] = v;
-    }
+    if (k >= n) break;
+    // top = r0[x0](1 - fx) + r0[x1] fx, bot likewise, top (1 - fy) + bot fy (src/resample.rs:66-71)
+    const float top = __fadd_rn(__fmul_rn(__ldg(src + o00), gx), __fmul_rn(__ldg(src + o01), cx.f));
+    const float bot = __fadd_rn(__fmul_rn(__ldg(src + o10), gx), __fmul_rn(__ldg(src + o11), cx.f));
+    float v = __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, cy.f));
+    if (add) v = __fadd_rn(v, __ldg(add + ((c0 + k) % add_c) * out_plane + yx));  // shared per image
+    *dst = v;
+    src += in_plane;
+    dst += out_plane;
   }
 }
 
@@ -341,7 +351,13 @@ namespace {
 constexpr int TM = 128;                      // tiles per CTA (MMA M)
 constexpr int TN = 32;                       // output channels per CTA (MMA N)
 constexpr int TK = 16;                       // input channels per slice (MMA K)
-constexpr int TC_WORKERS = 256;              // transform / epilogue threads
+#ifndef VK_CONV_TC_WORKERS
+#define VK_CONV_TC_WORKERS 512
+#endif
+constexpr int TC_WORKERS = VK_CONV_TC_WORKERS;  // transform / epilogue threads (256 or 512)
+constexpr int KPT = TK * TM / TC_WORKERS;       // input channels per worker per slice (8 or 4)
+constexpr int CPW = TN * 4 * 32 / TC_WORKERS;   // epilogue columns per worker warp (16 or 8)
+static_assert(KPT == 8 || KPT == 4, "workers");
 constexpr int TC_THREADS = TC_WORKERS + 32;  // + the MMA and copy warp
 constexpr int A_POS = TM * TK * 2;           // 4 KB: one position's V slice
 constexpr int B_POS = TN * TK * 2;           // 1 KB: one position's U slice
@@ -369,6 +385,11 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -463,39 +484,47 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       umma_commit(acc_done);
     }
   } else {
-    // ---- V slices: thread (tile row m, channel half kh); the CTA takes 128
+    // ---- V slices: thread (tile row m, channel group kh of KPT); the CTA takes 128
     // consecutive tiles in row-major order (rows of consecutive tiles load
     // best straight from global memory; L1 serves the patches' overlap)
-    const int m = tid & (TM - 1), kh = tid >> 7;
+    const int m = tid & (TM - 1), kh = tid / TM;
     const int lin_t = blockIdx.x * TM + m;
     const bool lin_ok = lin_t < tiles_x * tiles_y;
     const int lin_ty = lin_ok ? lin_t / tiles_x : 0, lin_tx = lin_ok ? lin_t % tiles_x : 0;
+    // the 4x4 patch's offsets in a channel plane (clamped into it) and which samples are inside
+    int roff[4], coff[4];
+    uint32_t inside = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int y = lin_ty * 2 - 1 + k, x = lin_tx * 2 - 1 + k;
+      roff[k] = min(max(y, 0), oh - 1) * iw;
+      coff[k] = min(max(x, 0), ow - 1);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int yj = lin_ty * 2 - 1 + j;
+        inside |= static_cast<uint32_t>(lin_ok && yj >= 0 && yj < oh && x >= 0 && x < ow) << (j * 4 + k);
+      }
+    }
+    const size_t plane_sz = static_cast<size_t>(ih) * iw;
     for (int s = 0; s < slices && ok; ++s) {
       const int b = s & 1;
-      uint32_t packed[16][4];
+      uint32_t packed[16][KPT / 2];
 #pragma unroll
-      for (int pr = 0; pr < 4; ++pr) {  // channel pairs of this thread's 8
+      for (int pr = 0; pr < KPT / 2; ++pr) {  // channel pairs of this thread's KPT
         float v2[2][16];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int icl = kh * 8 + pr * 2 + e;
+          const int icl = kh * KPT + pr * 2 + e;
           float d[16];
           const int ic = s * TK + icl;
-          const int y0 = lin_ty * 2 - 1, x0 = lin_tx * 2 - 1;
-          const bool live = ic < in_c && lin_ok;
-          const float* plane = in_img + static_cast<size_t>(live ? ic : 0) * ih * iw;
+          const uint32_t live = ic < in_c ? inside : 0u;
+          const float* plane = in_img + (ic < in_c ? ic : 0) * plane_sz;
 #pragma unroll
-          for (int dy = 0; dy < 4; ++dy)
-#pragma unroll
-            for (int dx = 0; dx < 4; ++dx) {
-              const int y = y0 + dy, x = x0 + dx;
-              float v = 0.0f;
-              if (live && y >= 0 && y < oh && x >= 0 && x < ow) {
-                v = __ldg(plane + static_cast<size_t>(y) * iw + x);
-                if constexpr (MODE == CONV_RELU) v = fmaxf(v, 0.0f);
-              }
-              d[dy * 4 + dx] = v;
-            }
+          for (int k = 0; k < 16; ++k) {
+            float v = __ldg(plane + roff[k >> 2] + coff[k & 3]);  // always inside the plane; zero outside the image
+            if constexpr (MODE == CONV_RELU) v = fmaxf(v, 0.0f);
+            d[k] = (live >> k) & 1u ? v : 0.0f;
+          }
           input_transform(d, v2[e]);
         }
 #pragma unroll
@@ -503,30 +532,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       // the slice's A buffer is free once the MMAs of slice s - 2 have finished
       if (s >= 2 && !(ok = mbar_wait(&ab_free[b], ((s >> 1) - 1) & 1, err, VK_DEV_TIMEOUT_OTHER))) break;
-      uint8_t* a = sA + b * A_SLICE + core_offset(m, kh * 8);
+      uint8_t* a = sA + b * A_SLICE + core_offset(m, kh * KPT);
 #pragma unroll
-      for (int p = 0; p < 16; ++p)
-        *reinterpret_cast<uint4*>(a + p * A_POS) = make_uint4(packed[p][0], packed[p][1], packed[p][2], packed[p][3]);
+      for (int p = 0; p < 16; ++p) {
+        if constexpr (KPT == 8)
+          *reinterpret_cast<uint4*>(a + p * A_POS) =
+              make_uint4(packed[p][0], packed[p][1 % (KPT / 2)], packed[p][2 % (KPT / 2)], packed[p][3 % (KPT / 2)]);
+        else
+          *reinterpret_cast<uint2*>(a + p * A_POS) = make_uint2(packed[p][0], packed[p][1]);
+      }
       fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
       mbar_arrive(&a_full[b]);
     }
-    // ---- epilogue: warp w reads lanes (tiles) of quarter w % 4, channels [16 (w / 4), +16)
+    // ---- epilogue: warp w reads lanes (tiles) of quarter w % 4, channels [CPW (w / 4), +CPW)
     if (ok && (ok = mbar_wait(acc_done, 0, err, VK_DEV_TIMEOUT_EPILOGUE))) {
       tc_fence_after();
       const int q = warp & 3, chh = warp >> 2;
       const int mt = q * 32 + lane;
       const int lt = blockIdx.x * TM + mt;
       const int ty = lt / tiles_x, tx = lt % tiles_x;
-      float acc[4][16];
+      float acc[4][CPW];
 #pragma unroll
       for (int o = 0; o < 4; ++o)
 #pragma unroll
-        for (int c = 0; c < 16; ++c) acc[o][c] = 0.0f;
+        for (int c = 0; c < CPW; ++c) acc[o][c] = 0.0f;
       constexpr float AT[2][4] = {{1.f, 1.f, 1.f, 0.f}, {0.f, 1.f, -1.f, -1.f}};
 #pragma unroll
       for (int p = 0; p < 16; ++p) {
-        uint32_t r[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + p * TN + chh * 16, r);
+        uint32_t r[CPW];
+        if constexpr (CPW == 16)
+          tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + p * TN + chh * CPW,
+                    *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+        else
+          tmem_ld8(tmem + (static_cast<uint32_t>(q * 32) << 16) + p * TN + chh * CPW,
+                   *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
         tmem_wait_ld();
         const int i = p >> 2, j = p & 3;
 #pragma unroll
@@ -536,7 +575,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const float cf = AT[dy][i] * AT[dx][j];
             if (cf == 0.0f) continue;
 #pragma unroll
-            for (int c = 0; c < 16; ++c)
+            for (int c = 0; c < CPW; ++c)
               acc[dy * 2 + dx][c] = cf > 0.0f ? acc[dy * 2 + dx][c] + __uint_as_float(r[c])
                                               : acc[dy * 2 + dx][c] - __uint_as_float(r[c]);
           }
@@ -545,8 +584,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int ty0 = ty * 2, tx0 = tx * 2;
         float* out_img = out + static_cast<size_t>(blockIdx.z) * out_c * oh * ow;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int oc = oc0 + chh * 16 + c;
+        for (int c = 0; c < CPW; ++c) {
+          const int oc = oc0 + chh * CPW + c;
           if (oc >= out_c) break;
           const float bb = bias ? __ldg(bias + oc) : 0.0f;
           float* plane = out_img + static_cast<size_t>(oc) * oh * ow;
