@@ -132,6 +132,7 @@ def cpu_reference_seconds_per_image(grid_h, grid_w, layers, reps: int = 1):
     threads) on one image, 12 layers, `reps` times; returns seconds/image."""
     from oracle import oracle
 
+    oracle.set_cpu_ref_threads(os.cpu_count())  # all host threads, whatever OMP_NUM_THREADS says
     T = grid_h * grid_w + 1
     x = np.random.default_rng(1).standard_normal((T, E), dtype=np.float32)
     times = []

@@ -385,6 +385,12 @@ def cpu_ref():
     return _REF
 
 
+def set_cpu_ref_threads(n: int) -> None:
+    """OpenMP threads of the timed CPU baseline (libvk_cpu_ref.so).  torchrun
+    exports OMP_NUM_THREADS=1 to every rank, so the baseline sets its own."""
+    cpu_ref().vko_set_threads(ctypes.c_int(n))
+
+
 def cpu_ref_encoder_layer(x, layer: dict, grid_h, grid_w, eps=1e-6, freq=100.0):
     """One block on the restated AVX-512 path; x [T, 768], modified copy returned."""
     x = _f32(x).copy()
