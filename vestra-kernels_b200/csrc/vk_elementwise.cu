@@ -41,9 +41,11 @@ __global__ void __launch_bounds__(EW_THREADS)
     k_layernorm_vec(const float* __restrict__ x, float* y, __nv_bfloat16* yb, int8_t* yq, __half* yd,
                     int rows, int cols, const float* __restrict__ g, const float* __restrict__ b, float eps) {
   grid_dependency_wait();  // x from the previous kernel is visible from here
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  // Rows run from the last to the first: the GEMM that wrote x finished with
+  // its last rows, which are the ones still in L2.
+  const int warp = rows - 1 - static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
-  if (warp >= rows) return;
+  if (warp < 0) return;
   const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(warp) * cols);
   float4 v[VPL];
   float s = 0.0f;
