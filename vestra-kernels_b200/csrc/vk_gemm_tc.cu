@@ -35,7 +35,6 @@ namespace vk {
 namespace {
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int GEMM_THREADS = 320;
-constexpr int EPI_THREADS = 256;
 constexpr int SLAB_BYTES = 128 * BK * 2;  // one 128-row operand slab per stage
 
 template <int MODE, bool PAIR>
@@ -51,13 +50,11 @@ struct Cfg {
   // bf16 outputs: the warp's whole 32 x WARP_COLS slice, one fence per tile
   static constexpr int WARP_BUFS = F32OUT ? 2 : (WARP_COLS / 32 > 2 ? WARP_COLS / 32 : 2);
   static constexpr int OUT_BYTES = 8 * WARP_BUFS * OUT_BUF;
-  static constexpr int BIAS_BYTES = 2 * TILE_N * 4;     // bias + scale of the tile
   static constexpr int STAGES = (F32OUT || PAIR) ? 4 : 5;
-  static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + OUT_BYTES + BIAS_BYTES + 256;
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + OUT_BYTES + 256;
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(EPI_THREADS) : "memory"); }
 
 // Writes this thread's 32 values as row `lane` of a 32-row staging tile in
 // the TMA 128-byte (f32) or 64-byte (bf16) swizzle, so that the 16-byte
@@ -245,9 +242,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * SLAB_BYTES;
   uint8_t* sOut = smem + C::STAGES * C::STAGE_BYTES;  // 1024-aligned
-  float* sBias = reinterpret_cast<float*>(sOut + C::OUT_BYTES);
-  float* sScale = sBias + C::TILE_N;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sScale + C::TILE_N);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + C::OUT_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -370,7 +365,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int ew = warp - 2;        // 0..7
     const int quad = warp & 3;      // TMEM lanes [32*quad, 32*quad + 32) are this warp's
     const int chalf = ew >> 2;      // which half of the tile's columns
-    const int et = threadIdx.x - 64;
     uint8_t* stage = sOut + ew * C::WARP_BUFS * C::OUT_BUF;
     int sb = 0;
     int it = 0;
@@ -380,13 +374,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t aphase = (it >> 1) & 1;
       const int m0 = (tile / n_tiles) * C::TILE_M;
       const int n0 = (tile % n_tiles) * C::TILE_N;
-      // bias / scale of this tile's columns into shared memory (all 8 warps)
-      epi_sync();
-      for (int i = et; i < C::TILE_N; i += EPI_THREADS) {
-        if (epi.bias) sBias[i] = __ldg(epi.bias + n0 + i);
-        if (epi.scale) sScale[i] = __ldg(epi.scale + n0 + i);
-      }
-      epi_sync();
       if (!mbar_wait(&tfull[acc], aphase, err, VK_DEV_TIMEOUT_EPILOGUE)) {
         ok = false;  // every epilogue warp gives up at the same tile
         break;
@@ -397,7 +384,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * C::TILE_N + c_off);
       epilogue_part<MODE, C::WARP_COLS>(epi, &tmO0, &tmO1, &tmO2, M, N, row0, n0 + c_off, tbase,
-                                        epi.bias ? sBias + c_off : nullptr, epi.scale ? sScale + c_off : nullptr,
+                                        // bias / scale straight from global memory (L1): no
+                                        // per-tile barrier across the epilogue warps
+                                        epi.bias ? epi.bias + n0 + c_off : nullptr,
+                                        epi.scale ? epi.scale + n0 + c_off : nullptr,
                                         stage, sb, lane, [&] {
                                           tc_fence_before();
                                           __syncwarp();
