@@ -50,7 +50,9 @@ struct Cfg {
   // bf16 outputs: the warp's whole 32 x WARP_COLS slice, one fence per tile
   static constexpr int WARP_BUFS = F32OUT ? 2 : (WARP_COLS / 32 > 2 ? WARP_COLS / 32 : 2);
   static constexpr int OUT_BYTES = 8 * WARP_BUFS * OUT_BUF;
-  static constexpr int STAGES = (F32OUT || PAIR) ? 4 : 5;
+  // as many K stages as shared memory holds (at most 6)
+  static constexpr int STAGES_FIT = static_cast<int>((232448 - 1024 - 256 - OUT_BYTES) / STAGE_BYTES);
+  static constexpr int STAGES = STAGES_FIT < 6 ? STAGES_FIT : 6;
   static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + OUT_BYTES + 256;
   static_assert(SMEM <= 232448, "shared memory budget");
 };
