@@ -266,12 +266,16 @@ def dpt_consumers(vk, ctx, B, gh, gw, reps=5):
     for mname, m in (("bf16", vk.MATH_BF16), ("f32", vk.MATH_F32)):
         f = vk.WinogradF2Filter(ctx, wt, ci, co, math=m)
         ms = timed(lambda: vk.conv3x3_batched(x, B, h, w, f, bias, y, ctx=ctx))
+        direct = 2.0 * 9 * ci * co * h * w * B / (ms / 1e3) / 1e12
         wino = 2.0 * 16 * ci * co * ((h + 1) // 2) * ((w + 1) // 2) * B / (ms / 1e3) / 1e12
-        res["conv3x3_%dx%d_%dx%d_%s" % (ci, co, h, w, mname)] = {
-            "ms": round(ms, 4), "winograd_tflops": wino,
-            "frac": wino / (peaks["bf16_sustained"] if m == vk.MATH_BF16 else FP32_SIMT_NOMINAL),
-            "of": "measured bf16 sustained (tensor)" if m == vk.MATH_BF16 else "nominal fp32 SIMT",
-            "direct_equiv_tflops": 2.0 * 9 * ci * co * h * w * B / (ms / 1e3) / 1e12}
+        if m == vk.MATH_BF16:  # implicit GEMM on the tensor cores: the direct convolution's FLOPs
+            res["conv3x3_%dx%d_%dx%d_bf16" % (ci, co, h, w)] = {
+                "ms": round(ms, 4), "tflops": direct, "frac": direct / peaks["bf16_sustained"],
+                "of": "measured bf16 sustained (tensor)", "includes": "the channels-last bf16 copy of the input"}
+        else:  # Winograd F(2x2, 3x3) on the SIMT cores: its transform-domain products
+            res["conv3x3_%dx%d_%dx%d_f32" % (ci, co, h, w)] = {
+                "ms": round(ms, 4), "winograd_tflops": wino, "frac": wino / FP32_SIMT_NOMINAL,
+                "of": "nominal fp32 SIMT", "direct_equiv_tflops": direct}
     del x, y
     c, ih, iw, oh, ow = DPT_RESIZE
     x = torch.randn(B * c * ih * iw, device="cuda")
@@ -291,10 +295,9 @@ def dpt_consumers(vk, ctx, B, gh, gw, reps=5):
         f = vk.WinogradF2Filter(ctx, wt, ci, co, math=m)
         ms = timed(lambda: vk.conv3x3_batched(x, B, ih, iw, f, bias, y, resize_to=(oh, ow), add=add, ctx=ctx))
         res["resize_ac_conv3x3_%dx%d_to_%dx%d_%s" % (ci, co, oh, ow, mname)] = {
-            "ms": round(ms, 4),
-            "winograd_tflops": 2.0 * 16 * ci * co * ((oh + 1) // 2) * ((ow + 1) // 2) * B / (ms / 1e3) / 1e12}
-    res["note"] = ("outside `value`. Convolutions: bf16 math = tensor-core Winograd products (f32 transforms), "
-                   "f32 math = the reference's f32 arithmetic on the SIMT cores (nominal peak %.1f TFLOP/s: "
+            "ms": round(ms, 4), "direct_equiv_tflops": 2.0 * 9 * ci * co * oh * ow * B / (ms / 1e3) / 1e12}
+    res["note"] = ("outside `value`. Convolutions: bf16 math = implicit GEMM on the tensor cores (direct FLOPs), "
+                   "f32 math = the reference's Winograd arithmetic on the SIMT cores (nominal peak %.1f TFLOP/s: "
                    "148 SMs x 128 lanes x 2 x 1965 MHz); resize / transpose against measured HBM" % FP32_SIMT_NOMINAL)
     return res
 

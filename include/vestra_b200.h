@@ -286,11 +286,12 @@ int vk_bilinear_resize_align_corners_f32(vk_ctx* ctx, const float* input, size_t
 typedef struct vk_conv3x3 vk_conv3x3;
 /* weight_host: OIHW [out_c, in_c, 3, 3] f32. */
 int vk_conv3x3_prepare(vk_ctx* ctx, const float* weight_host, size_t in_c, size_t out_c, vk_conv3x3** out);
-/* As vk_conv3x3_prepare with a math mode: VK_MATH_F32 (the SIMT kernel
- * above) or VK_MATH_BF16 -- the 16 transform-domain products on the tensor
- * cores with V and U rounded to bf16 and f32 accumulation (1e-2 relative
- * L2 bar, the precision class of the encoder's bf16 math); the transforms
- * and the resize stay f32. */
+/* As vk_conv3x3_prepare with a math mode: VK_MATH_F32 (the reference's
+ * Winograd F(2x2, 3x3) arithmetic) or VK_MATH_BF16 -- the convolution as an
+ * implicit GEMM on the tensor cores over bf16 inputs and weights with f32
+ * accumulation (1e-2 relative L2 bar, the precision class of the encoder's
+ * bf16 math).  bf16 math uses the context's workspace for a channels-last
+ * copy of the input (images * h * w * in_c rounded up to 64, bf16). */
 int vk_conv3x3_prepare_math(vk_ctx* ctx, const float* weight_host, size_t in_c, size_t out_c, int math,
                             vk_conv3x3** out);
 /* conv3x3_winograd_f2_prepared / _prepared_relu_input (src/conv.rs:282-302,

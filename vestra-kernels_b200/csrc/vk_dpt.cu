@@ -13,16 +13,18 @@
 // operations in its order (explicit round-to-nearest intrinsics, so nothing
 // is contracted into an FMA): bit-exact.
 //
-// The convolution (f32 math) is one kernel per (4 x 8 tiles of 2x2 outputs,
-// 32 output channels).  Per 16-channel slice it builds the transformed input
-// V = B^T d B of its tiles in shared memory (ReLU on the samples where
-// asked), stages the matching slice of the prepared filter U, and
-// accumulates the 16 transform-domain products M_p = V_p U_p in registers:
-// each thread owns one of the 16 positions for 8 tiles x 8 channels.  The
-// output transform A^T M A then runs from shared memory and writes the 2x2
-// outputs with the bias.  bf16 math runs the products on the tensor cores
-// (k_conv3x3_wino_tc below).  The resize-fused form resizes (and adds) into
-// the context workspace with the resize kernel, then convolves.
+// f32 math: the reference's Winograd F(2x2, 3x3) (k_conv3x3_wino), one
+// kernel per (4 x 8 tiles of 2x2 outputs, 32 output channels).  Per
+// 16-channel slice it builds the transformed input V = B^T d B of its tiles
+// in shared memory (ReLU on the samples where asked), stages the matching
+// slice of the prepared filter U, and accumulates the 16 transform-domain
+// products M_p = V_p U_p in registers: each thread owns one of the 16
+// positions for 8 tiles x 8 channels.  The output transform A^T M A then
+// runs from shared memory and writes the 2x2 outputs with the bias.
+// bf16 math: the convolution as an implicit GEMM on the tensor cores
+// (k_conv3x3_igemm) over a channels-last bf16 copy of the input.  The
+// resize-fused form resizes (and adds) first: into the workspace in f32 for
+// f32 math, straight into the channels-last bf16 operand for bf16 math.
 #include "vestra_b200.h"
 #include "vk_abi_internal.h"
 #include "vk_common.cuh"
@@ -35,7 +37,9 @@ struct vk_conv3x3 {
   int math = VK_MATH_F32;
   size_t in_c = 0, out_c = 0;
   float* u = nullptr;           // f32 math: [16][in_c][out_c]
-  __nv_bfloat16* ub = nullptr;  // bf16 math: [out_c / 32][in_c / 16][16][32 x 16 core-matrix tile]
+  __nv_bfloat16* wd = nullptr;  // bf16 math: [ocp][9 shifts][icp]
+  int bn = 0;                   // bf16 math: output channels per tile (32, 64 or 128)
+  size_t icp = 0, ocp = 0;
 };
 
 namespace {
@@ -93,17 +97,6 @@ __device__ __forceinline__ Coord ac_coord(int dst, int len_in, int len_out) {
   float f = b == a ? 0.0f : __fsub_rn(src, static_cast<float>(a));
   f = fminf(fmaxf(f, 0.0f), 1.0f);
   return {a, b, f};
-}
-
-// top = r0[x0](1 - fx) + r0[x1] fx, bot likewise, top (1 - fy) + bot fy
-// (src/resample.rs:66-71)
-__device__ __forceinline__ float blend(const float* __restrict__ plane, int iw, const Coord& y, const Coord& x) {
-  const float gx = __fsub_rn(1.0f, x.f), gy = __fsub_rn(1.0f, y.f);
-  const float* r0 = plane + static_cast<size_t>(y.i0) * iw;
-  const float* r1 = plane + static_cast<size_t>(y.i1) * iw;
-  const float top = __fadd_rn(__fmul_rn(__ldg(r0 + x.i0), gx), __fmul_rn(__ldg(r0 + x.i1), x.f));
-  const float bot = __fadd_rn(__fmul_rn(__ldg(r1 + x.i0), gx), __fmul_rn(__ldg(r1 + x.i1), x.f));
-  return __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, y.f));
 }
 
 // One CTA per (64 columns of an output row, 8 channels): the source
@@ -338,273 +331,214 @@ constexpr size_t DIM_MAX = size_t(1) << 20;
 
 }  // namespace
 
-// ---------------------------------------------------------------- conv on the tensor cores (bf16 math)
-// The 16 position products M_p = V_p U_p run as tcgen05 MMAs: per CTA 128
-// tiles (M) x 32 output channels (N) x 16 positions, accumulated in TMEM
-// (16 x 32 = all 512 columns).  K runs over 16-channel slices: 256 worker
-// threads build the slice's V (bf16, core-matrix K-major layout) in shared
-// memory, while one thread streams the prepared bf16 U slices in with bulk
-// copies and issues the 16 MMAs of the previous slice.  The epilogue reads
-// each tile row's 16 positions from TMEM and applies A^T M A in registers.
+// ---------------------------------------------------------------- direct conv on the tensor cores (bf16 math)
+// out[oc][y][x] = bias[oc] + sum over (ky, kx, ic) of W[oc][ic][ky][kx] * in[ic][y + ky - 1][x + kx - 1]
+// as an implicit GEMM: M = a block of 8 x 16 output pixels, N = BN output
+// channels, K = 9 kernel shifts x the (padded) input channels.  The input is
+// first rewritten channels-last in bf16 (k_to_nhwc_bf16); every K block is
+// then one TMA box of 64 channels x 16 x 8 pixels at the shifted position
+// (rows and columns outside the image read as zero: the padding), so the
+// 128-byte-swizzled A tile is a plain K-major operand.  W is packed
+// [oc][shift][ic] in bf16.  One tile per CTA: warp 0 loads, warp 1 issues
+// tcgen05 MMAs into TMEM, warps 2..5 (one per TMEM lane quadrant = 32
+// pixels) write the f32 NCHW output with the bias.
 namespace {
 
-constexpr int TM = 128;                      // tiles per CTA (MMA M)
-constexpr int TN = 32;                       // output channels per CTA (MMA N)
-constexpr int TK = 16;                       // input channels per slice (MMA K)
-#ifndef VK_CONV_TC_WORKERS
-#define VK_CONV_TC_WORKERS 512
-#endif
-constexpr int TC_WORKERS = VK_CONV_TC_WORKERS;  // transform / epilogue threads (256 or 512)
-constexpr int KPT = TK * TM / TC_WORKERS;       // input channels per worker per slice (8 or 4)
-constexpr int CPW = TN * 4 * 32 / TC_WORKERS;   // epilogue columns per worker warp (16 or 8)
-static_assert(KPT == 8 || KPT == 4, "workers");
-constexpr int TC_THREADS = TC_WORKERS + 32;  // + the MMA and copy warp
-constexpr int A_POS = TM * TK * 2;           // 4 KB: one position's V slice
-constexpr int B_POS = TN * TK * 2;           // 1 KB: one position's U slice
-constexpr int A_SLICE = 16 * A_POS, B_SLICE = 16 * B_POS;
-constexpr size_t TC_SMEM = 1024 + 2 * (A_SLICE + B_SLICE) + 128;
+constexpr int IG_BY = 8, IG_BX = 16;  // output pixels per tile: 8 rows x 16 columns (MMA M = 128)
+constexpr int IG_KC = 64;             // input channels per K block (128-byte rows)
+constexpr int IG_THREADS = 192;       // producer, MMA, 4 epilogue warps
+constexpr int IG_A_BYTES = 128 * IG_KC * 2;
 
-// K-major operand without swizzle: core matrices of 8 rows x 16 bytes; the
-// two along K (a 16-element slice) are 128 bytes apart (LBO), 8-row groups
-// 256 bytes apart (SBO).  Row r, element k at (r/8)*256 + (k/8)*128 + (r%8)*16 + (k%8)*2.
-__device__ __forceinline__ uint64_t desc_kmajor_core(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>(128u >> 4) << 16;  // LBO
-  d |= static_cast<uint64_t>(256u >> 4) << 32;  // SBO
-  d |= static_cast<uint64_t>(1u) << 46;         // sm_100 descriptor version; layout 0 = no swizzle
-  return d;
+// K stages: 3 at BN = 128 (two CTAs per SM), 4 below
+template <int BN>
+__host__ __device__ constexpr int ig_stages() {
+  return BN >= 128 ? 3 : 4;
 }
-__host__ __device__ constexpr int core_offset(int r, int k) { return (r / 8) * 256 + (k / 8) * 128 + (r % 8) * 16 + (k % 8) * 2; }
-
-// plain bulk copy global -> shared (no tensor map, no multicast)
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
+template <int BN>
+constexpr size_t ig_smem() {
+  return 1024 + static_cast<size_t>(ig_stages<BN>()) * (IG_A_BYTES + BN * IG_KC * 2) + 256;
 }
 
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* desc, uint64_t* bar, int32_t c0, int32_t c1,
+                                            int32_t c2, int32_t c3) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
 }
 
-// U f32 [16][in_c][out_c] -> bf16 [out_c / 32][slices][16 positions][32 x 16 core-matrix tile], zero-padded
-__global__ void k_pack_u_bf16(const float* __restrict__ u, __nv_bfloat16* __restrict__ ub, int in_c, int out_c,
-                              int slices, int ocb) {
-  const size_t total = static_cast<size_t>(ocb) * slices * 16 * TN * TK;
+// [images][C][H][W] f32 -> [images][H][W][Cp] bf16 (channels >= C zero), ReLU on request;
+// 32 x 32 (channel, column) tiles through shared memory.
+__global__ void k_to_nhwc_bf16(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, int C, int Cp, int H,
+                               int W, int relu) {
+  __shared__ float t[32][33];
+  const int x0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const int img = blockIdx.z / H, y = blockIdx.z - img * H;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  for (int r = ty; r < 32; r += 8) {
+    const int c = c0 + r, x = x0 + tx;
+    float v = 0.0f;
+    if (c < C && x < W) v = __ldg(in + ((static_cast<size_t>(img) * C + c) * H + y) * W + x);
+    t[r][tx] = relu ? fmaxf(v, 0.0f) : v;
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const int x = x0 + r, c = c0 + tx;
+    if (x < W && c < Cp) out[((static_cast<size_t>(img) * H + y) * W + x) * Cp + c] = __float2bfloat16_rn(t[tx][r]);
+  }
+}
+
+// Align-corners resize (+ add, shared by the images) of [images][C][ih][iw]
+// f32 straight into the channels-last bf16 operand [images][oh][ow][Cp]: a
+// thread takes one output pixel and 8 channels (one 16-byte store); the
+// blend is the f32 arithmetic of k_bilinear, rounded to bf16 at the end.
+__global__ void k_resize_ac_nhwc_bf16(const float* __restrict__ in, const float* __restrict__ add,
+                                      __nv_bfloat16* __restrict__ out, int C, int Cp, int ih, int iw, int oh, int ow) {
+  const int x = blockIdx.x * 32 + (threadIdx.x & 31);
+  const int y = blockIdx.y;
+  const int ngrp = Cp / 64;
+  const int img = blockIdx.z / ngrp;
+  const int c0 = (blockIdx.z - img * ngrp) * 64 + (threadIdx.x >> 5) * 8;
+  if (x >= ow) return;
+  const Coord cy = ac_coord(y, ih, oh), cx = ac_coord(x, iw, ow);
+  const int o00 = cy.i0 * iw + cx.i0, o01 = cy.i0 * iw + cx.i1, o10 = cy.i1 * iw + cx.i0, o11 = cy.i1 * iw + cx.i1;
+  const float gx = __fsub_rn(1.0f, cx.f), gy = __fsub_rn(1.0f, cy.f);
+  const size_t plane = static_cast<size_t>(ih) * iw, oplane = static_cast<size_t>(oh) * ow;
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 8; k += 2) {
+    float v[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int c = c0 + k + e;
+      float r = 0.0f;
+      if (c < C) {
+        const float* src = in + (static_cast<size_t>(img) * C + c) * plane;
+        const float top = __fadd_rn(__fmul_rn(__ldg(src + o00), gx), __fmul_rn(__ldg(src + o01), cx.f));
+        const float bot = __fadd_rn(__fmul_rn(__ldg(src + o10), gx), __fmul_rn(__ldg(src + o11), cx.f));
+        r = __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, cy.f));
+        if (add) r = __fadd_rn(r, __ldg(add + c * oplane + static_cast<size_t>(y) * ow + x));
+      }
+      v[e] = r;
+    }
+    w[k / 2] = pack_bf16x2(v[0], v[1]);
+  }
+  *reinterpret_cast<uint4*>(out + ((static_cast<size_t>(img) * oh + y) * ow + x) * Cp + c0) =
+      make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// OIHW f32 [out_c][in_c][3][3] -> bf16 [ocp][9][icp] (zero padded)
+__global__ void k_pack_w_direct(const float* __restrict__ w, __nv_bfloat16* __restrict__ wp, int in_c, int out_c,
+                                int icp, int ocp) {
+  const size_t total = static_cast<size_t>(ocp) * 9 * icp;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const int k = static_cast<int>(i % TK), n = static_cast<int>((i / TK) % TN);
-    const int p = static_cast<int>((i / (TK * TN)) % 16);
-    const size_t sb = i / (TK * TN * 16);
-    const int s = static_cast<int>(sb % slices), b = static_cast<int>(sb / slices);
-    const int ic = s * TK + k, oc = b * TN + n;
-    const float v = (ic < in_c && oc < out_c) ? u[(static_cast<size_t>(p) * in_c + ic) * out_c + oc] : 0.0f;
-    ub[sb * (16 * TN * TK) + p * (TN * TK) + core_offset(n, k) / 2] = __float2bfloat16_rn(v);
+    const int ic = static_cast<int>(i % icp), sft = static_cast<int>((i / icp) % 9), oc = static_cast<int>(i / (9 * icp));
+    const float v = (ic < in_c && oc < out_c) ? w[(static_cast<size_t>(oc) * in_c + ic) * 9 + sft] : 0.0f;
+    wp[i] = __float2bfloat16_rn(v);
   }
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(TC_THREADS, 1)
-    k_conv3x3_wino_tc(const float* __restrict__ input, const __nv_bfloat16* __restrict__ ub, const float* __restrict__ bias, float* __restrict__ out,
-                      int in_c, int ih, int iw, int oh, int ow, int out_c, int* err) {
+template <int BN>
+__global__ void __launch_bounds__(IG_THREADS)
+    k_conv3x3_igemm(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                    const float* __restrict__ bias, float* __restrict__ out, int H, int W, int out_c, int icp,
+                    int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;                   // [2][16][4 KB]
-  uint8_t* sB = smem + 2 * A_SLICE;     // [2][16][1 KB]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + 2 * B_SLICE);
-  uint64_t* a_full = bars;              // [2] count TC_WORKERS
-  uint64_t* b_full = bars + 2;          // [2] U slice landed
-  uint64_t* ab_free = bars + 4;         // [2] the slice's MMAs finished
-  uint64_t* acc_done = bars + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int slices = (in_c + TK - 1) / TK;
-  const int tiles_x = (ow + 1) / 2, tiles_y = (oh + 1) / 2;
-  const int ocb = blockIdx.y, oc0 = ocb * TN;
-  const float* in_img = input + static_cast<size_t>(blockIdx.z) * in_c * ih * iw;
-  const __nv_bfloat16* ub_blk = ub + static_cast<size_t>(ocb) * slices * (16 * TN * TK);
+  constexpr int B_BYTES = BN * IG_KC * 2;
+  constexpr int IG_STAGES = ig_stages<BN>();
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + IG_STAGES * IG_A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + IG_STAGES * B_BYTES);
+  uint64_t* empty = full + IG_STAGES;
+  uint64_t* done = empty + IG_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_x = (W + IG_BX - 1) / IG_BX, tiles_y = (H + IG_BY - 1) / IG_BY;
+  const int img = blockIdx.x / (tiles_x * tiles_y);
+  const int trem = blockIdx.x - img * tiles_x * tiles_y;
+  const int y0 = (trem / tiles_x) * IG_BY, x0 = (trem % tiles_x) * IG_BX;
+  const int n0 = blockIdx.y * BN;
+  const int kcb = icp / IG_KC, nk = 9 * kcb;
 
-  if (tid == 0) {
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&a_full[b], TC_WORKERS);
-      mbar_init(&b_full[b], 1);
-      mbar_init(&ab_free[b], 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < IG_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_done, 1);
+    mbar_init(done, 1);
     fence_mbar_init();
   }
-  if (warp == TC_WORKERS / 32) {
-    tmem_alloc(tmem_slot, 512);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, BN);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  bool ok = true;
 
-  if (warp == TC_WORKERS / 32) {
+  if (warp == 0) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(TM, TN);
-      auto load_u = [&](int s) {
-        mbar_arrive_expect_tx(&b_full[s & 1], B_SLICE);
-        bulk_load(sB + (s & 1) * B_SLICE, ub_blk + static_cast<size_t>(s) * (16 * TN * TK), B_SLICE, &b_full[s & 1]);
-      };
-      load_u(0);
-      if (slices > 1) load_u(1);
-      for (int s = 0; s < slices && ok; ++s) {
-        const int b = s & 1;
-        const uint32_t ph = (s >> 1) & 1;
-        if (!(ok = mbar_wait(&b_full[b], ph, err, VK_DEV_TIMEOUT_MMA))) break;
-        if (!(ok = mbar_wait(&a_full[b], ph, err, VK_DEV_TIMEOUT_MMA))) break;
-        tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + b * A_SLICE), b0 = smem_u32(sB + b * B_SLICE);
-#pragma unroll
-        for (int p = 0; p < 16; ++p)
-          umma_f16(tmem + p * TN, desc_kmajor_core(a0 + p * A_POS), desc_kmajor_core(b0 + p * B_POS), idesc,
-                   s > 0 ? 1u : 0u);
-        umma_commit(&ab_free[b]);
-        if (s + 2 < slices) {
-          if (!(ok = mbar_wait(&ab_free[b], ph, err, VK_DEV_TIMEOUT_MMA))) break;  // this slice's MMAs read sB[b]
-          load_u(s + 2);
-        }
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % IG_STAGES;
+        if (kb >= IG_STAGES && !mbar_wait(&empty[s], ((kb / IG_STAGES) - 1) & 1, err, VK_DEV_TIMEOUT_PRODUCER)) break;
+        const int sft = kb / kcb, cb = kb - sft * kcb;
+        const int ky = sft / 3, kx = sft - ky * 3;
+        mbar_arrive_expect_tx(&full[s], IG_A_BYTES + B_BYTES);
+        tma_load_4d(sA + s * IG_A_BYTES, &tmX, &full[s], cb * IG_KC, x0 + kx - 1, y0 + ky - 1, img);
+        tma_load_2d(sB + s * B_BYTES, &tmW, &full[s], sft * icp + cb * IG_KC, n0);
       }
-      umma_commit(acc_done);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, BN);
+      bool ok = true;
+      for (int kb = 0; kb < nk && ok; ++kb) {
+        const int s = kb % IG_STAGES;
+        if (!(ok = mbar_wait(&full[s], (kb / IG_STAGES) & 1, err, VK_DEV_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        const uint64_t adesc = smem_desc_k_sw128(smem_u32(sA + s * IG_A_BYTES));
+        const uint64_t bdesc = smem_desc_k_sw128(smem_u32(sB + s * B_BYTES));
+#pragma unroll
+        for (int k = 0; k < IG_KC / 16; ++k)
+          umma_f16(tmem, adesc + static_cast<uint64_t>(k * 2), bdesc + static_cast<uint64_t>(k * 2), idesc,
+                   (kb | k) > 0 ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(done);
     }
   } else {
-    // ---- V slices: thread (tile row m, channel group kh of KPT); the CTA takes 128
-    // consecutive tiles in row-major order (rows of consecutive tiles load
-    // best straight from global memory; L1 serves the patches' overlap)
-    const int m = tid & (TM - 1), kh = tid / TM;
-    const int lin_t = blockIdx.x * TM + m;
-    const bool lin_ok = lin_t < tiles_x * tiles_y;
-    const int lin_ty = lin_ok ? lin_t / tiles_x : 0, lin_tx = lin_ok ? lin_t % tiles_x : 0;
-    // the 4x4 patch's offsets in a channel plane (clamped into it) and which samples are inside
-    int roff[4], coff[4];
-    uint32_t inside = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int y = lin_ty * 2 - 1 + k, x = lin_tx * 2 - 1 + k;
-      roff[k] = min(max(y, 0), oh - 1) * iw;
-      coff[k] = min(max(x, 0), ow - 1);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int yj = lin_ty * 2 - 1 + j;
-        inside |= static_cast<uint32_t>(lin_ok && yj >= 0 && yj < oh && x >= 0 && x < ow) << (j * 4 + k);
-      }
-    }
-    const size_t plane_sz = static_cast<size_t>(ih) * iw;
-    for (int s = 0; s < slices && ok; ++s) {
-      const int b = s & 1;
-      uint32_t packed[16][KPT / 2];
-#pragma unroll
-      for (int pr = 0; pr < KPT / 2; ++pr) {  // channel pairs of this thread's KPT
-        float v2[2][16];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int icl = kh * KPT + pr * 2 + e;
-          float d[16];
-          const int ic = s * TK + icl;
-          const uint32_t live = ic < in_c ? inside : 0u;
-          const float* plane = in_img + (ic < in_c ? ic : 0) * plane_sz;
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            float v = __ldg(plane + roff[k >> 2] + coff[k & 3]);  // always inside the plane; zero outside the image
-            if constexpr (MODE == CONV_RELU) v = fmaxf(v, 0.0f);
-            d[k] = (live >> k) & 1u ? v : 0.0f;
-          }
-          input_transform(d, v2[e]);
-        }
-#pragma unroll
-        for (int p = 0; p < 16; ++p) packed[p][pr] = pack_bf16x2(v2[0][p], v2[1][p]);
-      }
-      // the slice's A buffer is free once the MMAs of slice s - 2 have finished
-      if (s >= 2 && !(ok = mbar_wait(&ab_free[b], ((s >> 1) - 1) & 1, err, VK_DEV_TIMEOUT_OTHER))) break;
-      uint8_t* a = sA + b * A_SLICE + core_offset(m, kh * KPT);
-#pragma unroll
-      for (int p = 0; p < 16; ++p) {
-        if constexpr (KPT == 8)
-          *reinterpret_cast<uint4*>(a + p * A_POS) =
-              make_uint4(packed[p][0], packed[p][1 % (KPT / 2)], packed[p][2 % (KPT / 2)], packed[p][3 % (KPT / 2)]);
-        else
-          *reinterpret_cast<uint2*>(a + p * A_POS) = make_uint2(packed[p][0], packed[p][1]);
-      }
-      fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
-      mbar_arrive(&a_full[b]);
-    }
-    // ---- epilogue: warp w reads lanes (tiles) of quarter w % 4, channels [CPW (w / 4), +CPW)
-    if (ok && (ok = mbar_wait(acc_done, 0, err, VK_DEV_TIMEOUT_EPILOGUE))) {
+    // pixel r = 32 (warp % 4) + lane of the tile: (y0 + r / 16, x0 + r % 16)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int y = y0 + r / IG_BX, x = x0 + r % IG_BX;
+    const bool inside = y < H && x < W;
+    if (mbar_wait(done, 0, err, VK_DEV_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
-      const int q = warp & 3, chh = warp >> 2;
-      const int mt = q * 32 + lane;
-      const int lt = blockIdx.x * TM + mt;
-      const int ty = lt / tiles_x, tx = lt % tiles_x;
-      float acc[4][CPW];
+      float* o = out + ((static_cast<size_t>(img) * out_c + n0) * H + y) * W + x;
+      const size_t plane = static_cast<size_t>(H) * W;
 #pragma unroll
-      for (int o = 0; o < 4; ++o)
-#pragma unroll
-        for (int c = 0; c < CPW; ++c) acc[o][c] = 0.0f;
-      constexpr float AT[2][4] = {{1.f, 1.f, 1.f, 0.f}, {0.f, 1.f, -1.f, -1.f}};
-#pragma unroll
-      for (int p = 0; p < 16; ++p) {
-        uint32_t r[CPW];
-        if constexpr (CPW == 16)
-          tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + p * TN + chh * CPW,
-                    *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-        else
-          tmem_ld8(tmem + (static_cast<uint32_t>(q * 32) << 16) + p * TN + chh * CPW,
-                   *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, v);
         tmem_wait_ld();
-        const int i = p >> 2, j = p & 3;
+        if (!inside) continue;
 #pragma unroll
-        for (int dy = 0; dy < 2; ++dy)
-#pragma unroll
-          for (int dx = 0; dx < 2; ++dx) {
-            const float cf = AT[dy][i] * AT[dx][j];
-            if (cf == 0.0f) continue;
-#pragma unroll
-            for (int c = 0; c < CPW; ++c)
-              acc[dy * 2 + dx][c] = cf > 0.0f ? acc[dy * 2 + dx][c] + __uint_as_float(r[c])
-                                              : acc[dy * 2 + dx][c] - __uint_as_float(r[c]);
-          }
-      }
-      if (ty < tiles_y && tx < tiles_x) {
-        const int ty0 = ty * 2, tx0 = tx * 2;
-        float* out_img = out + static_cast<size_t>(blockIdx.z) * out_c * oh * ow;
-#pragma unroll
-        for (int c = 0; c < CPW; ++c) {
-          const int oc = oc0 + chh * CPW + c;
-          if (oc >= out_c) break;
-          const float bb = bias ? __ldg(bias + oc) : 0.0f;
-          float* plane = out_img + static_cast<size_t>(oc) * oh * ow;
-#pragma unroll
-          for (int dy = 0; dy < 2; ++dy)
-#pragma unroll
-            for (int dx = 0; dx < 2; ++dx) {
-              const int y = ty0 + dy, x = tx0 + dx;
-              if (y < oh && x < ow) plane[static_cast<size_t>(y) * ow + x] = acc[dy * 2 + dx][c] + bb;
-            }
+        for (int j = 0; j < 32; ++j) {
+          const int oc = n0 + c * 32 + j;
+          if (oc < out_c) o[(c * 32 + j) * plane] = __uint_as_float(v[j]) + (bias ? __ldg(bias + oc) : 0.0f);
         }
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == TC_WORKERS / 32) {
+  if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, BN);
   }
 }
 
@@ -695,24 +629,28 @@ extern "C" int vk_conv3x3_prepare_math(vk_ctx* ctx, const float* weight_host, si
     e = cudaGetLastError();
   }
   if (e == cudaSuccess && math == VK_MATH_BF16) {
-    const int slices = static_cast<int>((in_c + TK - 1) / TK), ocb = static_cast<int>((out_c + TN - 1) / TN);
-    const size_t n = static_cast<size_t>(ocb) * slices * 16 * TN * TK;
-    e = cudaMalloc(&cv->ub, n * sizeof(__nv_bfloat16));
+    // the implicit-GEMM form: W as [ocp][9 shifts][icp] bf16
+    cv->bn = out_c <= 32 ? 32 : (out_c <= 64 ? 64 : 128);
+    cv->icp = (in_c + IG_KC - 1) / IG_KC * IG_KC;
+    cv->ocp = (out_c + cv->bn - 1) / cv->bn * cv->bn;
+    const size_t nw = cv->ocp * 9 * cv->icp;
+    if (e == cudaSuccess) e = cudaMalloc(&cv->wd, nw * sizeof(__nv_bfloat16));
     if (e == cudaSuccess) {
-      k_pack_u_bf16<<<static_cast<int>((n + DT_THREADS - 1) / DT_THREADS < 4096 ? (n + DT_THREADS - 1) / DT_THREADS : 4096),
-                      DT_THREADS, 0, ctx->stream>>>(cv->u, cv->ub, (int)in_c, (int)out_c, slices, ocb);
+      k_pack_w_direct<<<static_cast<int>((nw + DT_THREADS - 1) / DT_THREADS < 4096 ? (nw + DT_THREADS - 1) / DT_THREADS
+                                                                                  : 4096),
+                        DT_THREADS, 0, ctx->stream>>>(w, cv->wd, (int)in_c, (int)out_c, (int)cv->icp, (int)cv->ocp);
       e = cudaGetLastError();
     }
   }
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (w) cudaFree(w);
-  if (e == cudaSuccess && cv->ub) {  // bf16 math keeps only the packed filter
+  if (e == cudaSuccess && cv->wd) {  // bf16 math keeps only the packed filter
     cudaFree(cv->u);
     cv->u = nullptr;
   }
   if (e != cudaSuccess) {
     if (cv->u) cudaFree(cv->u);
-    if (cv->ub) cudaFree(cv->ub);
+    if (cv->wd) cudaFree(cv->wd);
     delete cv;
     return vk_cuda_status(e, "vk_conv3x3_prepare");
   }
@@ -728,25 +666,61 @@ extern "C" int vk_conv3x3_release(vk_conv3x3* conv) {
   if (!conv) return VK_OK;
   cudaSetDevice(conv->device);
   if (conv->u) cudaFree(conv->u);
-  if (conv->ub) cudaFree(conv->ub);
+  if (conv->wd) cudaFree(conv->wd);
   delete conv;
   return VK_OK;
+}
+
+template <int BN>
+static int igemm_launch(vk_ctx* ctx, const vk_conv3x3* cv, size_t images, const __nv_bfloat16* x_nhwc, size_t h,
+                        size_t w, const float* bias, float* out, const char* name) {
+  CUtensorMap tx, tw;
+  const uint64_t xd[4] = {cv->icp, w, h, images};
+  const uint64_t xs[3] = {cv->icp * 2, w * cv->icp * 2, h * w * cv->icp * 2};
+  const uint32_t xb[4] = {IG_KC, IG_BX, IG_BY, 1};
+  if (!make_tmap_nd(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x_nhwc, 4, xd, xs, xb, CU_TENSOR_MAP_SWIZZLE_128B))
+    return vk_fail(VK_ERR_CUDA, "%s: input tensor map", name);
+  const uint64_t wdim[2] = {9 * cv->icp, cv->ocp};
+  const uint64_t wst[1] = {9 * cv->icp * 2};
+  const uint32_t wb[2] = {IG_KC, BN};
+  if (!make_tmap_nd(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cv->wd, 2, wdim, wst, wb, CU_TENSOR_MAP_SWIZZLE_128B))
+    return vk_fail(VK_ERR_CUDA, "%s: filter tensor map", name);
+  const void* fn = reinterpret_cast<const void*>(k_conv3x3_igemm<BN>);
+  VK_TRY_CUDA(ensure_smem_limit(fn, static_cast<int>(ig_smem<BN>())), name);
+  const size_t tiles = ((h + IG_BY - 1) / IG_BY) * ((w + IG_BX - 1) / IG_BX) * images;
+  const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(cv->ocp / BN));
+  k_conv3x3_igemm<BN><<<grid, IG_THREADS, ig_smem<BN>(), ctx->stream>>>(tx, tw, bias, out, (int)h, (int)w,
+                                                                       (int)cv->out_c, (int)cv->icp, ctx->d_err);
+  return vk_cuda_status(cudaGetLastError(), name);
+}
+
+static int igemm_dispatch(vk_ctx* ctx, const vk_conv3x3* cv, size_t images, const __nv_bfloat16* xn, size_t h,
+                          size_t w, const float* bias, float* out, const char* name) {
+  switch (cv->bn) {
+    case 32: return igemm_launch<32>(ctx, cv, images, xn, h, w, bias, out, name);
+    case 64: return igemm_launch<64>(ctx, cv, images, xn, h, w, bias, out, name);
+    default: return igemm_launch<128>(ctx, cv, images, xn, h, w, bias, out, name);
+  }
+}
+
+// bf16 math: channels-last bf16 copy of the input (ReLU applied there) in the
+// workspace, then the implicit-GEMM convolution
+static int direct_conv(vk_ctx* ctx, const vk_conv3x3* cv, size_t images, const float* input, size_t h, size_t w,
+                       bool relu, const float* bias, float* out, const char* name) {
+  VK_TRY(ctx_reserve(ctx, images * h * w * cv->icp * sizeof(__nv_bfloat16)));
+  __nv_bfloat16* xn = static_cast<__nv_bfloat16*>(ctx->ws);
+  const dim3 g((unsigned)((w + 31) / 32), (unsigned)((cv->icp + 31) / 32), (unsigned)(images * h));
+  if (g.z > 65535 || g.y > 65535) return vk_fail(VK_UNSUPPORTED_SHAPE, "%s: images x height above 65535", name);
+  k_to_nhwc_bf16<<<g, 256, 0, ctx->stream>>>(input, xn, (int)cv->in_c, (int)cv->icp, (int)h, (int)w, relu ? 1 : 0);
+  VK_TRY_CUDA(cudaGetLastError(), name);
+  return igemm_dispatch(ctx, cv, images, xn, h, w, bias, out, name);
 }
 
 template <int MODE>
 static int conv_launch(vk_ctx* ctx, const vk_conv3x3* cv, size_t images, const float* input, size_t h, size_t w,
                        const float* bias, float* out, const char* name) {
-  const size_t tiles = ((h + 1) / 2) * ((w + 1) / 2);
-  if (cv->math == VK_MATH_BF16) {
-    const void* fn = reinterpret_cast<const void*>(k_conv3x3_wino_tc<MODE>);
-    VK_TRY_CUDA(ensure_smem_limit(fn, static_cast<int>(TC_SMEM)), name);
-    const dim3 grid(static_cast<unsigned>((tiles + TM - 1) / TM), static_cast<unsigned>((cv->out_c + TN - 1) / TN),
-                    static_cast<unsigned>(images));
-    k_conv3x3_wino_tc<MODE><<<grid, TC_THREADS, TC_SMEM, ctx->stream>>>(input, cv->ub, bias, out, (int)cv->in_c,
-                                                                        (int)h, (int)w, (int)h, (int)w,
-                                                                        (int)cv->out_c, ctx->d_err);
-    return vk_cuda_status(cudaGetLastError(), name);
-  }
+  if (cv->math == VK_MATH_BF16)
+    return direct_conv(ctx, cv, images, input, h, w, MODE == CONV_RELU, bias, out, name);
   const size_t blocks = ((h + 1) / 2 + TBY - 1) / TBY * (((w + 1) / 2 + TBX - 1) / TBX);
   const void* fn = reinterpret_cast<const void*>(k_conv3x3_wino<MODE>);
   VK_TRY_CUDA(ensure_smem_limit(fn, static_cast<int>(CONV_SMEM)), name);
@@ -799,6 +773,18 @@ extern "C" int vk_conv3x3_resize_ac_forward_batched(vk_ctx* ctx, const vk_conv3x
   // the gathers).  Same operations in the same order as the reference's
   // fused form, so the result is the one of resize, add, conv in sequence.
   const size_t planes = images * conv->in_c;
+  if (conv->math == VK_MATH_BF16) {
+    // bf16 math: the resize (+ add) writes the channels-last bf16 operand
+    // of the implicit-GEMM convolution directly
+    VK_TRY(ctx_reserve(ctx, images * oh * ow * conv->icp * sizeof(__nv_bfloat16)));
+    __nv_bfloat16* xn = static_cast<__nv_bfloat16*>(ctx->ws);
+    const dim3 g((unsigned)((ow + 31) / 32), (unsigned)oh, (unsigned)(images * (conv->icp / 64)));
+    if (g.y > 65535 || g.z > 65535) return vk_fail(VK_UNSUPPORTED_SHAPE, "%s: shape out of range", name);
+    k_resize_ac_nhwc_bf16<<<g, 256, 0, ctx->stream>>>(input, add, xn, (int)conv->in_c, (int)conv->icp, (int)ih,
+                                                      (int)iw, (int)oh, (int)ow);
+    VK_TRY_CUDA(cudaGetLastError(), name);
+    return igemm_dispatch(ctx, conv, images, xn, oh, ow, bias, out, name);
+  }
   VK_TRY(ctx_reserve(ctx, planes * oh * ow * sizeof(float)));
   float* mid = static_cast<float*>(ctx->ws);
   VK_TRY(resize_launch(ctx, input, planes, ih, iw, oh, ow, add, conv->in_c, mid, true, name));

@@ -52,6 +52,11 @@ bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
                   uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
                   uint32_t box1, CUtensorMapSwizzle swz);
 
+// Any rank up to 5: dims[0] innermost; strides_bytes[i] is the stride of
+// dimension i + 1; out-of-range box elements read as zero.
+bool make_tmap_nd(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int rank, const uint64_t* dims,
+                  const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz);
+
 int num_sms();
 // Launch attributes for programmatic dependent launch (off with VK_NO_PDL).
 bool pdl_enabled();

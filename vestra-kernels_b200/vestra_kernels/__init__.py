@@ -436,7 +436,8 @@ class WinogradF2Filter:
     filter transformed once to U [16, in_c, out_c] on the device."""
 
     def __init__(self, ctx: Context, weight, in_c: int, out_c: int, math: int = MATH_F32):
-        """math: MATH_F32 (SIMT, the reference's f32 arithmetic) or MATH_BF16 (tensor-core products)."""
+        """math: MATH_F32 (the reference's f32 Winograd arithmetic on the SIMT cores) or MATH_BF16 (the
+        convolution as an implicit GEMM on the tensor cores, bf16 operands, f32 accumulation)."""
         import numpy as np
 
         w = np.ascontiguousarray(weight, dtype=np.float32)
