@@ -88,10 +88,10 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       mbar_init(&q_full[b], 1);
       mbar_init(&q_empty[b], 1);
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 128);
+      mbar_init(&p_full[b], 4);  // one arrival per softmax warp
       mbar_init(&o_done[b], 1);
     }
-    for (int b = 0; b < 4; ++b) mbar_init(&o_free[b], 128);
+    for (int b = 0; b < 4; ++b) mbar_init(&o_free[b], 4);
     for (int s = 0; s < AST; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -290,7 +290,8 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         tmem_st32(tb + COL_S + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[t]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
         l_run += l_blk;
       }
       if (!ok || !mbar_wait(&o_done[t], ct & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
@@ -304,7 +305,8 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       tmem_ld32(tb + col_o + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&o_free[t * 2 + (ct & 1)]);  // O is in registers: item ct+2 may overwrite it
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[t * 2 + (ct & 1)]);  // O is in registers: item ct+2 may overwrite it
       ++ct;
 #pragma unroll
       for (int d = 0; d < 64; ++d) o[d] *= inv;

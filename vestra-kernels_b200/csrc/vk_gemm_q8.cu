@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
     }
     for (int a = 0; a < QNACC; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], Q_EPI_THREADS);
+      mbar_init(&tempty[a], Q_EPI_THREADS / 32);  // one arrival per epilogue warp
     }
     fence_mbar_init();
   }
@@ -186,7 +186,8 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
         tmem_ld32(ta, r0);
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&tempty[buf]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
         const float4* wd4 = reinterpret_cast<const float4*>(sWd + b * QBN + cq * 32);
         // acc + (d_a * d_b) * isum, each step rounded (src/scalar.rs:47-52),
         // the multiplies two columns per packed f32x2 operation (IEEE
