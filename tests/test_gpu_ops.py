@@ -183,6 +183,18 @@ def test_linear_rejects_non_da3_shape(vk, ctx):
     assert float(out.abs().sum()) == 0.0
 
 
+def test_dimensions_beyond_32_bits_are_rejected(vk, ctx):
+    # The kernels index with 32-bit ints; the entry points refuse larger
+    # dimensions before touching any buffer (the pointers are never read).
+    import ctypes
+
+    lib, big, dummy = vk.lib(), 1 << 31, ctypes.c_void_p(16)
+    assert lib.vk_linear_f32_da3_base(ctx.handle, big, 768, 768, dummy, dummy, dummy) == vk.VK_UNSUPPORTED_SHAPE
+    assert "32-bit" in vk.last_error()
+    assert lib.vk_gemm_q8_0(ctx.handle, big, 128, 128, dummy, dummy, dummy) == vk.VK_UNSUPPORTED_SHAPE
+    assert lib.vk_layernorm(ctx.handle, dummy, big, 768, dummy, dummy, ctypes.c_float(1e-6)) == vk.VK_UNSUPPORTED_SHAPE
+
+
 def test_prepared_linear_chain_matches_reference_values(vk, ctx):
     """src/cuda.rs:1433-1447: two prepared linears run back to back (f32)."""
     import json

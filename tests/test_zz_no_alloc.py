@@ -54,3 +54,7 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     st = lib.vk_gemm_q8_0_noalloc(None, 4096, 3072, 3072, dummy, dummy, dummy)
     assert st == vk.VK_UNSUPPORTED_SHAPE
     assert "scratch" in vk.last_error()
+    # a row count whose byte count would wrap 64 bits is rejected, not run
+    st = lib.vk_gemm_q8_0_noalloc(None, 1 << 60, 128, 128, dummy, dummy, dummy)
+    assert st == vk.VK_UNSUPPORTED_SHAPE
+    assert "scratch" in vk.last_error()

@@ -224,6 +224,7 @@ extern "C" int vk_qkv_f32_da3_base(vk_ctx* ctx, size_t tokens, const float* inpu
                                    const float* bias, float* q, float* k, float* v) {
   VK_CTX_CHECK(ctx, "vk_qkv_f32_da3_base");
   if (tokens == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_qkv_f32_da3_base: tokens == 0");
+  VK_TRY(vk_dims_fit("vk_qkv_f32_da3_base", {tokens}));
   if (!input || !weight || !bias || !q || !k || !v)
     return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_qkv_f32_da3_base: NULL buffer");
   GemmEpi epi;
@@ -241,6 +242,7 @@ extern "C" int vk_linear_f32_da3_base(vk_ctx* ctx, size_t m, size_t n, size_t k,
   VK_CTX_CHECK(ctx, "vk_linear_f32_da3_base");
   if (m == 0 || !da3_projection(k, n))
     return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_linear_f32_da3_base: (m=%zu, k=%zu, n=%zu) is not a DA3-BASE projection", m, k, n);
+  VK_TRY(vk_dims_fit("vk_linear_f32_da3_base", {m}));
   if (!input || !weight || !output) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_linear_f32_da3_base: NULL buffer");
   GemmEpi epi;
   epi.out = output;
@@ -253,6 +255,7 @@ extern "C" int vk_linear_bias_scale_f32_da3_base(vk_ctx* ctx, size_t m, size_t n
   VK_CTX_CHECK(ctx, "vk_linear_bias_scale_f32_da3_base");
   if (m == 0 || !((k == 768 && n == 768) || (k == 3072 && n == 768)))
     return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_linear_bias_scale_f32_da3_base: (k=%zu, n=%zu) unsupported", k, n);
+  VK_TRY(vk_dims_fit("vk_linear_bias_scale_f32_da3_base", {m}));
   if (!a || !b || !bias || !scale || !c) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_linear_bias_scale_f32_da3_base: NULL buffer");
   GemmEpi epi;
   epi.bias = bias;
@@ -283,6 +286,7 @@ extern "C" int vk_flash_attention_f32_da3_base(vk_ctx* ctx, const float* query, 
                                                size_t heads, size_t tokens, float* output) {
   VK_CTX_CHECK(ctx, "vk_flash_attention_f32_da3_base");
   if (heads == 0 || tokens == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_flash_attention_f32_da3_base: empty shape");
+  VK_TRY(vk_dims_fit("vk_flash_attention_f32_da3_base", {heads, tokens}));
   if (!query || !key || !value || !output) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_flash_attention_f32_da3_base: NULL buffer");
   return attention64(ctx, query, key, value, heads, tokens, output, "vk_flash_attention_f32_da3_base");
 }
@@ -293,6 +297,7 @@ extern "C" int vk_qk_norm_rope_f32_da3_base(vk_ctx* ctx, float* q, float* k, siz
                                             float epsilon) {
   VK_CTX_CHECK(ctx, "vk_qk_norm_rope_f32_da3_base");
   if (heads == 0 || tokens == 0) return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_qk_norm_rope_f32_da3_base: empty shape");
+  VK_TRY(vk_dims_fit("vk_qk_norm_rope_f32_da3_base", {heads, tokens}));
   if (!q || !k || !q_gamma || !q_beta || !k_gamma || !k_beta || !positions_yx)
     return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_qk_norm_rope_f32_da3_base: NULL buffer");
   VK_TRY(ctx_reserve(ctx, tokens * 64 * sizeof(float) + 256));
@@ -309,6 +314,7 @@ extern "C" int vk_attention(vk_ctx* ctx, const float* q, const float* k, const f
   VK_CTX_CHECK(ctx, "vk_attention");
   if (heads == 0 || n == 0) return VK_OK;
   if (!q || !k || !v || !out) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_attention: NULL buffer");
+  VK_TRY(vk_dims_fit("vk_attention", {heads, n}));
   if (head_dim == 64) return attention64(ctx, q, k, v, heads, n, out, "vk_attention");
   if (head_dim != 8 && head_dim != 16 && head_dim != 32)
     return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_attention: head_dim %zu (supported: 8, 16, 32, 64)", head_dim);
@@ -321,6 +327,7 @@ extern "C" int vk_rope2d(vk_ctx* ctx, float* x, size_t heads, size_t n, size_t h
   if (head_dim % 4 != 0) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_rope2d: head_dim must be divisible by 4, got %zu", head_dim);
   if (heads == 0 || n == 0 || head_dim == 0) return VK_OK;
   if (!x || !pos_yx) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_rope2d: NULL buffer");
+  VK_TRY(vk_dims_fit("vk_rope2d", {heads, n, head_dim}));
   VK_TRY(ctx_reserve(ctx, n * head_dim * sizeof(float) + 256));
   float* rot = static_cast<float*>(ctx->ws);
   VK_TRY(upload_rotations_from_device_positions(ctx, pos_yx, n, head_dim, freq, rot));
@@ -332,6 +339,7 @@ extern "C" int vk_layernorm(vk_ctx* ctx, float* x, size_t rows, size_t cols, con
   VK_CTX_CHECK(ctx, "vk_layernorm");
   if (rows == 0 || cols == 0) return VK_OK;
   if (!x || !gamma || !beta) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_layernorm: NULL buffer");
+  VK_TRY(vk_dims_fit("vk_layernorm", {rows, cols}));
   return vk_cuda_status(layernorm_f32(x, x, nullptr, nullptr, nullptr, (int)rows, (int)cols, gamma, beta, eps, ctx->stream),
                         "vk_layernorm");
 }
@@ -385,6 +393,7 @@ static int gemm_q8_blocks(vk_ctx* ctx, size_t m, size_t n, size_t k, const vk_bl
   if (k == 0 || k % 128 != 0 || n % 128 != 0)
     return vk_fail(VK_UNSUPPORTED_SHAPE, "%s: needs k %% 128 == 0 and n %% 128 == 0 (k=%zu, n=%zu)", name, k, n);
   if (!a_q || !b_q || (!c && !dots)) return vk_fail(VK_ERR_INVALID_ARGUMENT, "%s: NULL buffer", name);
+  VK_TRY(vk_dims_fit(name, {m, n, k}));
   const size_t nb = k / 32;
   auto layout = [&](Arena& ar, void** p) {
     p[0] = ar.get<int8_t>(m * k);
@@ -544,6 +553,7 @@ extern "C" int vk_prepare_linear_q8_0(vk_ctx* ctx, size_t k, size_t n, const vk_
 extern "C" int vk_linear_run(vk_ctx* ctx, const vk_linear* lin, size_t m, const float* input, float* output) {
   VK_CTX_CHECK(ctx, "vk_linear_run");
   if (!lin || !input || !output) return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_linear_run: NULL argument");
+  VK_TRY(vk_dims_fit("vk_linear_run", {m}));
   if (m == 0) return VK_OK;
   const size_t k = lin->k, n = lin->n;
   GemmEpi epi;

@@ -5,6 +5,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <climits>
+#include <initializer_list>
 #include <map>
 #include <tuple>
 #include <vector>
@@ -86,6 +88,16 @@ struct vk_encoder {
 };
 
 int vk_fail(int status, const char* fmt, ...);
+
+// The kernels take their dimensions as 32-bit ints: an entry point rejects
+// any dimension beyond INT_MAX with VK_UNSUPPORTED_SHAPE instead of letting a
+// narrowing cast truncate it.
+inline int vk_dims_fit(const char* name, std::initializer_list<size_t> dims) {
+  for (size_t d : dims)
+    if (d > static_cast<size_t>(INT_MAX))
+      return vk_fail(VK_UNSUPPORTED_SHAPE, "%s: dimension %zu exceeds the 32-bit range of the kernels", name, d);
+  return VK_OK;
+}
 int vk_cuda_status(cudaError_t e, const char* what);
 int ctx_reserve(vk_ctx* ctx, size_t bytes);
 

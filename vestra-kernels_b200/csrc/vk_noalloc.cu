@@ -67,6 +67,10 @@ extern "C" int vk_gemm_q8_0_noalloc(void* stream, size_t m, size_t n, size_t k, 
   if (k == 0 || k % 128 != 0 || n % 128 != 0)
     return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_gemm_q8_0_noalloc: needs k %% 128 == 0 and n %% 128 == 0 (k=%zu, n=%zu)",
                    k, n);
+  // bound each factor first so that the byte counts below cannot wrap
+  if (m > VK_NOALLOC_SCRATCH_BYTES || n > VK_NOALLOC_SCRATCH_BYTES || k > VK_NOALLOC_SCRATCH_BYTES)
+    return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_gemm_q8_0_noalloc: m=%zu n=%zu k=%zu exceeds the fixed %u-byte scratch", m,
+                   n, k, VK_NOALLOC_SCRATCH_BYTES);
   const size_t nb = k / 32;
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
   const size_t a_q_bytes = up(m * k), b_q_bytes = up(n * k), a_d_bytes = up(m * nb * 2), b_d_bytes = up(n * nb * 2);
