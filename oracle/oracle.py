@@ -351,21 +351,27 @@ def _layer_struct(layer: dict):
     return keep, _Layer(**{kk: _p(vv) for kk, vv in keep.items()})
 
 
-def encoder_layer(x, layer: dict, grid_h, grid_w, heads=12, eps=1e-6, freq=100.0, bf16_points=False):
-    """One DA3-BASE block composed from the restated operators; x [T, E]."""
+def encoder_layer(x, layer: dict, grid_h, grid_w, heads=12, eps=1e-6, freq=100.0, bf16_points=False,
+                  q8_points=False):
+    """One DA3-BASE block composed from the restated operators; x [T, E].
+
+    bf16_points rounds to bf16 (v to f16) where the bf16 kernels store;
+    q8_points runs the projections as gemm_q8_0 over Q8_0 weights and
+    activations, where the Q8_0 kernels quantise."""
+    assert not (bf16_points and q8_points)
     x = _f32(x).copy()
     t, e = x.shape
     ffn = np.shape(layer["fc1_w"])[1]
     keep, st = _layer_struct(layer)
     lib().vko_encoder_layer(_p(x), _sz(t), _sz(grid_h), _sz(grid_w), _sz(e), _sz(heads), _sz(ffn),
                             ctypes.byref(st), ctypes.c_float(eps), ctypes.c_float(freq),
-                            ctypes.c_int(1 if bf16_points else 0))
+                            ctypes.c_int(2 if q8_points else (1 if bf16_points else 0)))
     return x
 
 
-def encoder(x, layers, grid_h, grid_w, heads=12, eps=1e-6, freq=100.0, bf16_points=False):
+def encoder(x, layers, grid_h, grid_w, heads=12, eps=1e-6, freq=100.0, bf16_points=False, q8_points=False):
     for layer in layers:
-        x = encoder_layer(x, layer, grid_h, grid_w, heads, eps, freq, bf16_points)
+        x = encoder_layer(x, layer, grid_h, grid_w, heads, eps, freq, bf16_points, q8_points)
     return x
 
 

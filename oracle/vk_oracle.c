@@ -533,13 +533,43 @@ static float* copy_maybe_bf16(const float* src, size_t n, int bf16) {
   return d;
 }
 
+static void round_f16_buf(float* x, size_t n) {
+  for (size_t i = 0; i < n; ++i) x[i] = vko_f16_to_f32(vko_f16_from_f32(x[i]));
+}
+
+/* Q8_0 weights as Kernels::gemm_q8_0 takes them: the [K, N] input-major
+ * weight transposed to [N, K] rows (src/dispatch.rs:85-90), each row
+ * quantised with quantize_row_q8_0 (src/q8_0_dot.rs:27-46). */
+static vko_block_q8_0* quantize_weight_q8(const float* w_kn, size_t k, size_t n) {
+  float* row = (float*)malloc(sizeof(float) * k);
+  vko_block_q8_0* blocks = (vko_block_q8_0*)malloc(sizeof(vko_block_q8_0) * n * (k / VKO_QK8_0));
+  for (size_t j = 0; j < n; ++j) {
+    for (size_t p = 0; p < k; ++p) row[p] = w_kn[p * n + j];
+    vko_quantize_row_q8_0(row, k / VKO_QK8_0, blocks + j * (k / VKO_QK8_0));
+  }
+  free(row);
+  return blocks;
+}
+
+/* c [m, n] = gemm_q8_0(quantize(a), wq): activations quantised per 32-block
+ * of each row, then the reference's block-ascending f32 fold
+ * (src/scalar.rs:25-56). */
+static void linear_q8(size_t m, size_t n, size_t k, const float* a, const vko_block_q8_0* wq, float* c) {
+  const size_t nb = k / VKO_QK8_0;
+  vko_block_q8_0* aq = (vko_block_q8_0*)malloc(sizeof(vko_block_q8_0) * m * nb);
+  for (size_t i = 0; i < m; ++i) vko_quantize_row_q8_0(a + i * k, nb, aq + i * nb);
+  vko_gemm_q8_0(m, n, k, aq, wq, c);
+  free(aq);
+}
+
 /* pre-LN -> QKV (+bias) -> 2D RoPE on Q,K (cls at (0,0), so unrotated) ->
  * attention -> out-proj (+bias) * LS1 + residual -> LN -> fc1 (+bias) -> GELU
- * -> fc2 (+bias) * LS2 + residual. */
+ * -> fc2 (+bias) * LS2 + residual.  `points` as documented in vk_oracle.h. */
 void vko_encoder_layer(float* x, size_t tokens, size_t grid_h, size_t grid_w, size_t embed,
                        size_t heads, size_t ffn, const vko_layer* w, float eps, float rope_freq,
-                       int bf16_points) {
+                       int points) {
   const size_t T = tokens, E = embed, F = ffn;
+  const int bf16 = points == VKO_POINTS_BF16, q8 = points == VKO_POINTS_Q8_0;
   float* h = (float*)malloc(sizeof(float) * T * E);
   float* q = (float*)malloc(sizeof(float) * T * E);
   float* k = (float*)malloc(sizeof(float) * T * E);
@@ -559,45 +589,82 @@ void vko_encoder_layer(float* x, size_t tokens, size_t grid_h, size_t grid_w, si
     pos[2 * t + 1] = pos[2 * (t % TV) + 1];
   }
 
-  float* wqkv = copy_maybe_bf16(w->qkv_w, E * 3 * E, bf16_points);
-  float* wo = copy_maybe_bf16(w->proj_w, E * E, bf16_points);
-  float* w1 = copy_maybe_bf16(w->fc1_w, E * F, bf16_points);
-  float* w2 = copy_maybe_bf16(w->fc2_w, F * E, bf16_points);
+  float *wqkv = NULL, *wo = NULL, *w1 = NULL, *w2 = NULL;
+  vko_block_q8_0 *qqkv = NULL, *qo = NULL, *q1 = NULL, *q2 = NULL;
+  if (q8) {
+    qqkv = quantize_weight_q8(w->qkv_w, E, 3 * E);
+    qo = quantize_weight_q8(w->proj_w, E, E);
+    q1 = quantize_weight_q8(w->fc1_w, E, F);
+    q2 = quantize_weight_q8(w->fc2_w, F, E);
+  } else {
+    wqkv = copy_maybe_bf16(w->qkv_w, E * 3 * E, bf16);
+    wo = copy_maybe_bf16(w->proj_w, E * E, bf16);
+    w1 = copy_maybe_bf16(w->fc1_w, E * F, bf16);
+    w2 = copy_maybe_bf16(w->fc2_w, F * E, bf16);
+  }
 
   memcpy(h, x, sizeof(float) * T * E);
   vko_layernorm(h, T, E, w->ln1_g, w->ln1_b, eps);
-  if (bf16_points) round_bf16_buf(h, T * E);
-  vko_qkv(T, heads, h, wqkv, w->qkv_b, q, k, v);
+  if (bf16) round_bf16_buf(h, T * E);
+  if (q8) {
+    float* tmp = (float*)malloc(sizeof(float) * T * 3 * E);
+    linear_q8(T, 3 * E, E, h, qqkv, tmp);
+    for (size_t t = 0; t < T; ++t)
+      for (size_t col = 0; col < 3 * E; ++col) {
+        const size_t g = col / E, hh = (col % E) / 64, d = col % 64;
+        float* dst = g == 0 ? q : (g == 1 ? k : v);
+        dst[(hh * T + t) * 64 + d] = tmp[t * 3 * E + col] + w->qkv_b[col];
+      }
+    free(tmp);
+  } else {
+    vko_qkv(T, heads, h, wqkv, w->qkv_b, q, k, v);
+  }
   if (w->qn_g != NULL) {
     vko_qk_norm_rope(q, k, heads, T, w->qn_g, w->qn_b, w->kn_g, w->kn_b, pos, rope_freq, eps);
   } else {
     vko_rope2d(q, heads, T, 64, pos, rope_freq);
     vko_rope2d(k, heads, T, 64, pos, rope_freq);
   }
-  if (bf16_points) {
+  if (bf16 || q8) {
     round_bf16_buf(q, T * E);
     round_bf16_buf(k, T * E);
-    round_bf16_buf(v, T * E);
+    round_f16_buf(v, T * E);
   }
   vko_attention_naive(q, k, v, heads, T, 64, att);
   for (size_t hh = 0; hh < heads; ++hh)
     for (size_t t = 0; t < T; ++t)
       for (size_t d = 0; d < 64; ++d) tok[t * E + hh * 64 + d] = att[(hh * T + t) * 64 + d];
-  if (bf16_points) round_bf16_buf(tok, T * E);
-  vko_linear_bias_scale(T, E, E, tok, wo, w->proj_b, w->ls1, o);
+  if (bf16) round_bf16_buf(tok, T * E);
+  if (q8) {
+    linear_q8(T, E, E, tok, qo, o);
+    for (size_t i = 0; i < T; ++i)
+      for (size_t j = 0; j < E; ++j) o[i * E + j] = (o[i * E + j] + w->proj_b[j]) * w->ls1[j];
+  } else {
+    vko_linear_bias_scale(T, E, E, tok, wo, w->proj_b, w->ls1, o);
+  }
   vko_add(x, o, T * E);
 
   memcpy(h, x, sizeof(float) * T * E);
   vko_layernorm(h, T, E, w->ln2_g, w->ln2_b, eps);
-  if (bf16_points) round_bf16_buf(h, T * E);
-  gemm_fma_rows(T, F, E, h, w1, f);
+  if (bf16) round_bf16_buf(h, T * E);
+  if (q8)
+    linear_q8(T, F, E, h, q1, f);
+  else
+    gemm_fma_rows(T, F, E, h, w1, f);
   vko_add_bias_rows(f, T, F, w->fc1_b);
   vko_gelu(f, T * F);
-  if (bf16_points) round_bf16_buf(f, T * F);
-  vko_linear_bias_scale(T, E, F, f, w2, w->fc2_b, w->ls2, o);
+  if (bf16) round_bf16_buf(f, T * F);
+  if (q8) {
+    linear_q8(T, E, F, f, q2, o);
+    for (size_t i = 0; i < T; ++i)
+      for (size_t j = 0; j < E; ++j) o[i * E + j] = (o[i * E + j] + w->fc2_b[j]) * w->ls2[j];
+  } else {
+    vko_linear_bias_scale(T, E, F, f, w2, w->fc2_b, w->ls2, o);
+  }
   vko_add(x, o, T * E);
 
   free(wqkv); free(wo); free(w1); free(w2);
+  free(qqkv); free(qo); free(q1); free(q2);
   free(h); free(q); free(k); free(v); free(att); free(tok); free(o); free(f); free(pos);
 }
 

@@ -96,9 +96,18 @@ void vko_linear_bias_scale(size_t m, size_t n, size_t k, const float* a, const f
                            const float* bias, const float* scale, float* c);
 
 /* One DA3-BASE ViT block composed from the restated operators (the engine's
- * composition, which is not in the reference crate).  When bf16_points is
- * non-zero the inputs of every matrix product and the tensors the B200
- * kernels store in bf16 are rounded to bf16 at the same points. */
+ * composition, which is not in the reference crate).  `points` selects the
+ * arithmetic at the points where the B200 kernels store narrow types:
+ *   VKO_POINTS_F32   all f32;
+ *   VKO_POINTS_BF16  the inputs of every matrix product and the stored
+ *                    activations rounded to bf16 (v to f16, the type of the
+ *                    attention P V product);
+ *   VKO_POINTS_Q8_0  projections through gemm_q8_0 on Q8_0 weights and
+ *                    Q8_0-quantised activations (src/scalar.rs:25-56,
+ *                    src/q8_0_dot.rs:27-46); q, k bf16 and v f16. */
+#define VKO_POINTS_F32 0
+#define VKO_POINTS_BF16 1
+#define VKO_POINTS_Q8_0 2
 typedef struct {
   const float *ln1_g, *ln1_b;
   const float *qkv_w, *qkv_b;   /* [E, 3E], [3E] */
@@ -118,7 +127,7 @@ typedef struct {
  * view. */
 void vko_encoder_layer(float* x, size_t tokens, size_t grid_h, size_t grid_w, size_t embed,
                        size_t heads, size_t ffn, const vko_layer* w, float eps, float rope_freq,
-                       int bf16_points);
+                       int points);
 
 /* src/cuda.rs:295-316 vestra_patchify_nchw_f32: image [channels, height,
  * width] -> patches [(height/patch)(width/patch), channels * patch^2], each

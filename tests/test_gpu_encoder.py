@@ -1,11 +1,15 @@
 """GPU parity of the DA3-BASE encoder (vk_encoder_*) against the oracle's
 block composition on the same seeded random-init weights.
 
-Because LayerScale starts at 1e-5 the residual stream barely moves in one
-block, so the bars are stated on the block's *update* (out - in), which is
-what the kernels compute: relative L2 <= 1e-3 for bf16 math against the
-oracle fed the same bf16-rounded operands, <= 1e-5 for f32 math, and a
-looser bar for Q8_0 (quantised weights and activations against f32).
+The bars are stated on a block's *update* (out - in), which is what the
+kernels compute, with LayerScale 1 so the update is as large as the stream
+(at the DA3 init of 1e-5 the update sits below the f32 resolution of the
+residual it is added to).  Relative L2 per layer, at the DA3-BASE shapes:
+  bf16  <= 1e-3 against the oracle rounding to bf16 (v to f16) where the
+        kernels store;
+  f32   <= 1e-5 against the f32 oracle;
+  Q8_0  <= BAR["q8"] against the oracle composing the reference's Q8_0 ops
+        (quantize_row_q8_0, gemm_q8_0) at the kernels' quantisation points.
 """
 import numpy as np
 import pytest
@@ -61,22 +65,84 @@ def run_encoder(vk, ctx, layers, x, images, gh, gw, math):
     return out.cpu().numpy(), enc
 
 
-@pytest.mark.parametrize("math", ["bf16", "f32", "q8"])
+MATHS = ["bf16", "f32", "q8"]
+BAR = {"bf16": 1e-3, "f32": 1e-5, "q8": 1e-3}
+
+
+def math_mode(vk, math):
+    return {"bf16": vk.MATH_BF16, "f32": vk.MATH_F32, "q8": vk.MATH_Q8_0}[math]
+
+
+def oracle_points(math):
+    return {"bf16_points": math == "bf16", "q8_points": math == "q8"}
+
+
+@pytest.mark.parametrize("math", MATHS)
 def test_one_block_full_size(vk, ctx, oracle_lib, math):
     gh, gw = 24, 36
     T = gh * gw + 1
     layers = make_layers(1, 7, ls=1.0)  # LayerScale 1 so the update is visible
     x = np.random.default_rng(8).standard_normal((1, T, E)).astype(np.float32)
-    m = {"bf16": vk.MATH_BF16, "f32": vk.MATH_F32, "q8": vk.MATH_Q8_0}[math]
-    got, enc = run_encoder(vk, ctx, layers, x, 1, gh, gw, m)
-    ref = oracle_lib.encoder(x[0], layers, gh, gw, bf16_points=(math == "bf16"))
+    got, enc = run_encoder(vk, ctx, layers, x, 1, gh, gw, math_mode(vk, math))
+    ref = oracle_lib.encoder(x[0], layers, gh, gw, **oracle_points(math))
     err = rel_l2(got[0] - x[0], ref - x[0])
     print(f"encoder block math={math} update rel_l2={err:.3e} launches={enc.last_launches()}")
-    bar = {"bf16": 1e-3, "f32": 1e-5, "q8": 5e-2}[math]
-    if math == "bf16":
-        bar = 5e-3  # attention probabilities are rounded to bf16 inside the kernel
-    assert err < bar
-    assert rel_l2(got[0], ref) < (1e-2 if math == "q8" else 1e-3)
+    assert err < BAR[math]
+    assert rel_l2(got[0], ref) < BAR[math]
+
+
+@pytest.mark.parametrize("math", MATHS)
+def test_twelve_layers_per_layer_full_size(vk, ctx, oracle_lib, math):
+    """The 12-layer DA3-BASE encoder at 504x336 (24 x 36 patches, 865
+    tokens): every layer's update against the oracle layer fed the same
+    input (the GPU's own output of the layer before), and the 12-layer
+    forward equal to the chain of single-layer forwards."""
+    gh, gw = 24, 36
+    T = gh * gw + 1
+    layers = make_layers(12, 41, ls=1.0)
+    x0 = np.random.default_rng(42).standard_normal((1, T, E)).astype(np.float32)
+    m = math_mode(vk, math)
+    x = x0
+    errs = []
+    for layer in layers:
+        got, _ = run_encoder(vk, ctx, [layer], x, 1, gh, gw, m)
+        ref = oracle_lib.encoder_layer(x[0], layer, gh, gw, **oracle_points(math))
+        errs.append(rel_l2(got[0] - x[0], ref - x[0]))
+        x = got
+    print(f"12-layer {math} per-layer update rel_l2: " + " ".join(f"{e:.2e}" for e in errs))
+    assert max(errs) < BAR[math], errs
+    full, enc = run_encoder(vk, ctx, layers, x0, 1, gh, gw, m)
+    assert enc.last_launches() == 12 * (10 if math == "f32" else 7)
+    assert np.array_equal(full, x)
+
+
+@pytest.mark.parametrize("math", MATHS)
+def test_one_block_1008x672(vk, ctx, oracle_lib, math):
+    """One block at 1008x672: 48 x 72 patches + cls = 3457 tokens, the RoPE
+    grid 72 wide (src/specialized.rs:359-366) and 28 key blocks."""
+    gh, gw = 48, 72
+    T = gh * gw + 1
+    layers = make_layers(1, 51, ls=1.0)
+    x = np.random.default_rng(52).standard_normal((1, T, E)).astype(np.float32)
+    got, _ = run_encoder(vk, ctx, layers, x, 1, gh, gw, math_mode(vk, math))
+    ref = oracle_lib.encoder(x[0], layers, gh, gw, **oracle_points(math))
+    err = rel_l2(got[0] - x[0], ref - x[0])
+    print(f"encoder block 3457 tokens math={math} update rel_l2={err:.3e}")
+    assert err < BAR[math]
+
+
+def test_da3_layerscale_twelve_layers(vk, ctx, oracle_lib):
+    """BASELINE's random init (LayerScale 1e-5), 12 layers chained, bf16:
+    the whole output against the chained oracle."""
+    gh, gw = 24, 36
+    T = gh * gw + 1
+    layers = make_layers(12, 61, ls=1e-5)
+    x = np.random.default_rng(62).standard_normal((1, T, E)).astype(np.float32)
+    got, _ = run_encoder(vk, ctx, layers, x, 1, gh, gw, vk.MATH_BF16)
+    ref = oracle_lib.encoder(x[0], layers, gh, gw, bf16_points=True)
+    err = rel_l2(got[0], ref)
+    print(f"12-layer LayerScale 1e-5 output rel_l2={err:.3e}")
+    assert err < 1e-6
 
 
 def test_batch_images_independent(vk, ctx, oracle_lib):
@@ -90,6 +156,8 @@ def test_batch_images_independent(vk, ctx, oracle_lib):
 
 
 def test_twelve_layers_small_grid(vk, ctx, oracle_lib):
+    """Two 25-token images through 12 chained layers: a whole-stack bar,
+    since 12 chained bf16 layers compound their rounding."""
     gh, gw = 4, 6
     T = gh * gw + 1
     layers = make_layers(12, 11, ls=0.1)
@@ -98,8 +166,8 @@ def test_twelve_layers_small_grid(vk, ctx, oracle_lib):
     for i in range(2):
         ref = oracle_lib.encoder(x[i], layers, gh, gw, bf16_points=True)
         err = rel_l2(got[i] - x[i], ref - x[i])
-        print(f"12-layer image {i} update rel_l2={err:.3e}")
-        assert err < 1e-2
+        print(f"12-layer image {i} stacked update rel_l2={err:.3e}")
+        assert err < 3e-3
     assert enc.last_launches() == 12 * 7
 
 
@@ -157,40 +225,73 @@ def test_large_batch_matches_single_images(vk, ctx, oracle_lib):
         assert err < 1e-3, (i, err)
 
 
-@pytest.mark.parametrize("math", ["bf16", "f32"])
-def test_multiview_global_layers(vk, ctx, oracle_lib, math):
-    """Layers 1 and 3 attend across each pair of views (one sequence of
-    2 x 25 tokens, RoPE positions repeating per view); layers 0 and 2 within
-    each view.  Oracle: the same composition from the restated block."""
-    gh, gw, V = 4, 6, 2
+def oracle_views_layer(oracle_lib, views, layer, gh, gw, joint, bf):
+    """One layer over a group of views: jointly (a global layer) or per view."""
     T = gh * gw + 1
-    layers = make_layers(4, 21, ls=0.1)
-    x = np.random.default_rng(22).standard_normal((4, T, E)).astype(np.float32)
+    if joint:
+        out = oracle_lib.encoder_layer(np.concatenate(views), layer, gh, gw, bf16_points=bf)
+        return [out[i * T:(i + 1) * T] for i in range(len(views))]
+    return [oracle_lib.encoder_layer(v, layer, gh, gw, bf16_points=bf) for v in views]
+
+
+def per_layer_views(vk, ctx, oracle_lib, layers, x, gh, gw, V, global_layers, math, tag):
+    """Every layer of a multi-view stack against the oracle layer fed the
+    GPU's own input; the whole stack equal to the chained layers."""
     m = {"bf16": vk.MATH_BF16, "f32": vk.MATH_F32}[math]
-    enc = vk.Encoder(ctx, layers, math=m, views=V, global_layers=(1, 3))
+    bf = math == "bf16"
+    images = x.shape[0]
+    cur = x
+    errs = []
+    for li, layer in enumerate(layers):
+        g = li in global_layers
+        enc = vk.Encoder(ctx, [layer], math=m, views=V, global_layers=(0,) if g else ())
+        t = torch.from_numpy(cur).cuda()
+        out = torch.empty_like(t)
+        assert enc.forward(t, out, images, gh, gw)
+        ctx.synchronize()
+        got = out.cpu().numpy()
+        for grp in range(images // V):
+            views = [cur[grp * V + i] for i in range(V)]
+            ref = oracle_views_layer(oracle_lib, views, layer, gh, gw, g, bf)
+            for i in range(V):
+                img = grp * V + i
+                errs.append(rel_l2(got[img] - cur[img], ref[i] - cur[img]))
+        cur = got
+    print(f"{tag} {math}: per-layer update rel_l2 max {max(errs):.2e}")
+    assert max(errs) < BAR[math], errs
+    enc = vk.Encoder(ctx, layers, math=m, views=V, global_layers=tuple(global_layers))
     t = torch.from_numpy(x).cuda()
     out = torch.empty_like(t)
-    assert enc.forward(t, out, 4, gh, gw)
+    assert enc.forward(t, out, images, gh, gw)
     ctx.synchronize()
-    got = out.cpu().numpy()
-    bf = math == "bf16"
-    for g in range(2):
-        views = [x[2 * g + i].copy() for i in range(V)]
-        for li, layer in enumerate(layers):
-            if li in (1, 3):
-                joint = oracle_lib.encoder_layer(np.concatenate(views), layer, gh, gw, bf16_points=bf)
-                views = [joint[i * T:(i + 1) * T] for i in range(V)]
-            else:
-                views = [oracle_lib.encoder_layer(v, layer, gh, gw, bf16_points=bf) for v in views]
-        for i in range(V):
-            img = 2 * g + i
-            err = rel_l2(got[img] - x[img], views[i] - x[img])
-            print(f"multi-view {math} image {img}: update rel_l2 {err:.2e}")
-            assert err < (1e-2 if bf else 1e-5)
+    assert np.array_equal(out.cpu().numpy(), cur)
+    return enc, t
+
+
+@pytest.mark.parametrize("math", ["bf16", "f32"])
+def test_multiview_global_layers(vk, ctx, oracle_lib, math):
+    """Two views of 504x336 (one sequence of 2 x 865 tokens, RoPE positions
+    repeating per view) in global layers 1 and 2, per-view layer 0.
+    Oracle: the same composition from the restated block."""
+    gh, gw, V = 24, 36, 2
+    T = gh * gw + 1
+    layers = make_layers(3, 21, ls=1.0)
+    x = np.random.default_rng(22).standard_normal((2, T, E)).astype(np.float32)
+    enc, t = per_layer_views(vk, ctx, oracle_lib, layers, x, gh, gw, V, (1, 2), math, "multi-view")
     # an image count that is not whole groups is refused, output untouched
-    out2 = torch.zeros((3, T, E), device="cuda")
-    assert not enc.forward(t[:3].contiguous(), out2, 3, gh, gw)
+    out2 = torch.zeros((1, T, E), device="cuda")
+    assert not enc.forward(t[:1].contiguous(), out2, 1, gh, gw)
     assert float(out2.abs().sum()) == 0.0
+
+
+def test_multiview_small_grid(vk, ctx, oracle_lib):
+    """Four 25-token images as two pairs of views, global layers 1 and 3,
+    f32 (the bf16 bar is set at the DA3-BASE shapes above)."""
+    gh, gw, V = 4, 6, 2
+    T = gh * gw + 1
+    layers = make_layers(4, 25, ls=1.0)
+    x = np.random.default_rng(26).standard_normal((4, T, E)).astype(np.float32)
+    per_layer_views(vk, ctx, oracle_lib, layers, x, gh, gw, V, (1, 3), "f32", "multi-view 25")
 
 
 def add_qk_norm(layer, seed):
@@ -207,32 +308,16 @@ def add_qk_norm(layer, seed):
 def test_qk_norm_layers(vk, ctx, oracle_lib, math):
     """Layers 1 and 2 LayerNorm each q / k head before RoPE (DA3's late
     blocks, qk_norm_rope_f32_da3_base); layer 2 is also a global cross-view
-    layer.  Oracle: the restated block with the same options."""
-    gh, gw, V = 4, 6, 2
+    layer.  Two 504x336 views.  Oracle: the restated block with the same
+    options."""
+    gh, gw, V = 24, 36, 2
     T = gh * gw + 1
-    layers = make_layers(3, 31, ls=0.1)
+    layers = make_layers(3, 31, ls=1.0)
     layers[1] = add_qk_norm(layers[1], 32)
     layers[2] = add_qk_norm(layers[2], 33)
     x = np.random.default_rng(34).standard_normal((2, T, E)).astype(np.float32)
-    m = {"bf16": vk.MATH_BF16, "f32": vk.MATH_F32}[math]
-    enc = vk.Encoder(ctx, layers, math=m, views=V, global_layers=(2,))
-    t = torch.from_numpy(x).cuda()
+    enc, t = per_layer_views(vk, ctx, oracle_lib, layers, x, gh, gw, V, (2,), math, "qk-norm")
     out = torch.empty_like(t)
-    assert enc.forward(t, out, 2, gh, gw)
-    ctx.synchronize()
-    got = out.cpu().numpy()
-    bf = math == "bf16"
-    views = [x[0].copy(), x[1].copy()]
-    for li, layer in enumerate(layers):
-        if li == 2:
-            joint = oracle_lib.encoder_layer(np.concatenate(views), layer, gh, gw, bf16_points=bf)
-            views = [joint[:T], joint[T:]]
-        else:
-            views = [oracle_lib.encoder_layer(v, layer, gh, gw, bf16_points=bf) for v in views]
-    for i in range(2):
-        err = rel_l2(got[i] - x[i], views[i] - x[i])
-        print(f"qk-norm {math} image {i}: update rel_l2 {err:.2e}")
-        assert err < (1e-2 if bf else 1e-5)
     slots = enc.profile(t, out, 2, gh, gw)
     assert len(slots) == (10 if math == "f32" else 7) and all(s >= 0.0 for s in slots)
 

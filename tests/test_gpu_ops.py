@@ -267,7 +267,7 @@ def test_flash_attention_bf16(vk, ctx, oracle_lib, tokens, heads):
         got = host(out).reshape(q.shape)
         err = rel_l2(got, oracle_lib.attention_naive(q, k, v))
         print(f"bf16 attention tokens={tokens} rel_l2={err:.3e}")
-        assert err < 2e-3
+        assert err < 1e-3
     finally:
         ctx.set_math(vk.MATH_F32)
 
@@ -288,18 +288,19 @@ def test_flash_attention_bf16_logit_jumps(vk, ctx, oracle_lib, boost):
         got = host(out).reshape(q.shape)
         assert np.isfinite(got).all()
         err = rel_l2(got, oracle_lib.attention_naive(q, k, v))
-        assert err < 2e-3, err
+        assert err < 1e-3, err
     finally:
         ctx.set_math(vk.MATH_F32)
 
 
 # ---------------------------------------------------------------- norms, RoPE, pointwise
-@pytest.mark.parametrize("rows,cols", [(865, 768), (67, 64), (5, 100)])
+@pytest.mark.parametrize("rows,cols", [(865, 768), (67, 64), (5, 100), (20011, 768), (33, 3072)])
 def test_layernorm(vk, ctx, oracle_lib, rows, cols):
     x, g, b = rng_inputs(90 + cols, (rows, cols), (cols,), (cols,))
     t = dev(x)
     vk.layernorm(t, rows, cols, dev(g), dev(b), 1e-6, ctx=ctx)
-    assert rel_l2(host(t), oracle_lib.layernorm(x, g, b, 1e-6)) < 1e-6
+    # bit-exact: the same ascending folds and separately rounded operations
+    assert np.array_equal(host(t).reshape(rows, cols), oracle_lib.layernorm(x, g, b, 1e-6))
 
 
 def test_rope2d_bit_exact(vk, ctx, oracle_lib):
@@ -323,8 +324,8 @@ def test_qk_norm_rope(vk, ctx, oracle_lib):
     assert vk.qk_norm_rope_f32_da3_base(tq, tk, dev(g), dev(b), dev(g), dev(b), dev(pos.ravel(), torch.int64),
                                         100.0, 1e-6, ctx=ctx)
     rq, rk = oracle_lib.qk_norm_rope(q, k, g, b, g, b, pos, 100.0, 1e-6)
-    assert rel_l2(host(tq).reshape(q.shape), rq) < 1e-6
-    assert rel_l2(host(tk).reshape(k.shape), rk) < 1e-6
+    assert np.array_equal(host(tq).reshape(q.shape), rq)
+    assert np.array_equal(host(tk).reshape(k.shape), rk)
 
 
 def test_gelu_add_bias_layerscale(vk, ctx, oracle_lib):

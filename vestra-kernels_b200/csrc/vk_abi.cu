@@ -275,10 +275,10 @@ static int attention64(vk_ctx* ctx, const float* q, const float* k, const float*
   Arena ar{ctx->ws, 0};
   auto* q16 = ar.get<__nv_bfloat16>(n);
   auto* k16 = ar.get<__nv_bfloat16>(n);
-  auto* v16 = ar.get<__nv_bfloat16>(n);
+  auto* v16 = ar.get<__half>(n);  // V in f16, the type of the P V product
   VK_TRY_CUDA(cast_f32_bf16(q, q16, n, s), name);
   VK_TRY_CUDA(cast_f32_bf16(k, k16, n, s), name);
-  VK_TRY_CUDA(cast_f32_bf16(v, v16, n, s), name);
+  VK_TRY_CUDA(cast_f32_f16(v, v16, n, s), name);
   return vk_cuda_status(attention_bf16(q16, k16, v16, 1, (int)heads, (int)tokens, ATTN_OUT_HEAD_F32, out, nullptr, ctx->d_err, s), name);
 }
 

@@ -15,16 +15,18 @@
 //   warp 0      TMA: per item the Q tiles, then K and V blocks of 128 keys
 //               (AST-stage ring running across items)
 //   warp 1      TMEM owner; one lane issues, per key block j and tile t,
-//                 O_t     += P_t(j) V_j      (M=128, N=64, K=128; A = P_t from TMEM)
+//                 O_t     += P_t(j) V_j      (M=128, N=64, K=128; A = P_t from TMEM;
+//                                             P and V in f16: an 11-bit P keeps the
+//                                             P V rounding near 2e-4 relative)
 //                 S_t(j+1) = Q_t K_j+1^T     (M=128, N=128, K=64; A, B from smem)
 //               in that order: the tensor core runs MMAs in issue order, so
 //               S_t(j+1) overwrites P_t(j) only after O_t read it
 //   warps 2..5  softmax of tile 0, warps 6..9 of tile 1, one query row per
 //               thread: p = 2^(s*log2e/8 - m_ref) in one pass over S against
 //               the running reference (block 0's max), row sum, P -> TMEM as
-//               bf16 over S.  O accumulates in TMEM; a block whose row sums
-//               would overflow is redone against its own max with O
-//               rescaled.  Finally O / l is stored token-major bf16 / Q8_0 or
+//               f16 over S.  O accumulates in TMEM; a block whose row sum
+//               would leave the f16 range of P (2^15) is redone against its
+//               own max with O rescaled.  Finally O / l is stored token-major bf16 / Q8_0 or
 //               head-major f32.
 // TMEM per tile (256 columns): S / P [0, 128), O for even / odd items
 // [128, 192) / [192, 256).
@@ -51,7 +53,10 @@ constexpr uint32_t COL_S = 0, COL_O = 128, TILE_COLS = 256;  // S / P [0, 128), 
 constexpr size_t ATT_SMEM = 1024 + TILE_BYTES * (4 + 2 * AST) + 512;
 }  // namespace
 
-template <int OUT>
+// SPLIT: P is stored as two f16 halves, P = P_hi + P_lo (P_hi over S columns
+// [0, 64), P_lo over [64, 128)), and O += P_hi V + P_lo V, so the P V
+// product carries about 22 bits of P instead of 11.
+template <int OUT, bool SPLIT>
 __global__ void __launch_bounds__(A_THREADS, 1)
     k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, int heads, int tokens, int items, int tpi, void* out,
@@ -135,7 +140,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(128, 128);
-      constexpr uint32_t idO = idesc_bf16_bmn(128, 64);
+      constexpr uint32_t idO = idesc_f16_bmn(128, 64);
       auto issue_s = [&](int t, int qb, uint32_t st) {
         const uint64_t qdesc = smem_desc_k_sw128(smem_u32(sQ + (qb * 2 + t) * TILE_BYTES));
         const uint64_t kdesc = smem_desc_k_sw128(smem_u32(sK + st * TILE_BYTES));
@@ -177,6 +182,12 @@ __global__ void __launch_bounds__(A_THREADS, 1)
             for (int k = 0; k < AKV / 16; ++k)
               umma_f16_ts(base + COL_O + ob * 64, base + COL_S + static_cast<uint32_t>(k * 8),
                           vdesc + static_cast<uint64_t>(k * (2048 >> 4)), idO, (j | k) > 0 ? 1u : 0u);
+            if constexpr (SPLIT) {
+#pragma unroll
+              for (int k = 0; k < AKV / 16; ++k)
+                umma_f16_ts(base + COL_O + ob * 64, base + COL_S + 64 + static_cast<uint32_t>(k * 8),
+                            vdesc + static_cast<uint64_t>(k * (2048 >> 4)), idO, 1u);
+            }
             if (more) {
               issue_s(t, qb, (g + 1) % AST);
               umma_commit(&s_full[t]);  // also covers O_t(j)
@@ -234,7 +245,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           }
           return fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])) * sl2;
         };
-        // p = 2^(s * log2e / 8 - m) packed as bf16 pairs into pk; returns the row sum
+        // p = 2^(s * log2e / 8 - m) packed as f16 pairs into pk; returns the row sum
         uint32_t pk[64];
         auto exp_pass = [&](float m) -> float {
           float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
@@ -256,20 +267,99 @@ __global__ void __launch_bounds__(A_THREADS, 1)
                 pp.y = k0 + 1 < valid ? pp.y : 0.0f;
               }
               ps[i & 1] = fadd2(ps[i & 1], pp);
-              pk[c * 16 + i] = pack_bf16x2(pp.x, pp.y);
+              pk[c * 16 + i] = pack_f16x2(pp.x, pp.y);
             }
           }
           return (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y);
         };
+        if constexpr (SPLIT) {
+          // p = 2^(s log2e / 8 - m) as P_hi = f16(p) over columns [0, 64) and
+          // P_lo = f16(p - P_hi) over [64, 128).  The block max is taken first,
+          // so P can be written while S is still being read: keys [0, 64) are
+          // read first, their P_hi lands on columns already read, their P_lo
+          // waits in registers until columns [64, 128) have been read too.
+          auto exp_split = [&](float m) -> float {
+            float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+            const float2 scale2 = make_float2(sl2, sl2), shift2 = make_float2(-m, -m);
+            uint32_t lo_hold[32];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t rr[64];
+              tmem_ld32(tb + COL_S + h * 64, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+              tmem_ld32(tb + COL_S + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
+              tmem_wait_ld();
+              if (h == 1) {
+                tmem_st16(tb + COL_S + 64, *reinterpret_cast<uint32_t(*)[16]>(&lo_hold[0]));
+                tmem_st16(tb + COL_S + 80, *reinterpret_cast<uint32_t(*)[16]>(&lo_hold[16]));
+              }
+#pragma unroll
+              for (int sub = 0; sub < 2; ++sub) {
+                uint32_t hi16[16], lo16[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const int pi = sub * 16 + i;  // pair within this half
+                  const int k0 = h * 64 + 2 * pi;
+                  const float2 x = ffma2(make_float2(__uint_as_float(rr[2 * pi]), __uint_as_float(rr[2 * pi + 1])),
+                                         scale2, shift2);
+                  float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                  if (!full_block) {
+                    pp.x = k0 < valid ? pp.x : 0.0f;
+                    pp.y = k0 + 1 < valid ? pp.y : 0.0f;
+                  }
+                  ps[i & 1] = fadd2(ps[i & 1], pp);
+                  const __half2 hh = __floats2half2_rn(pp.x, pp.y);
+                  const float2 hf = __half22float2(hh);
+                  hi16[i] = *reinterpret_cast<const uint32_t*>(&hh);
+                  lo16[i] = pack_f16x2(pp.x - hf.x, pp.y - hf.y);
+                }
+                tmem_st16(tb + COL_S + h * 32 + sub * 16, hi16);
+                if (h == 1) {
+                  tmem_st16(tb + COL_S + 96 + sub * 16, lo16);
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) lo_hold[sub * 16 + i] = lo16[i];
+                }
+              }
+            }
+            return (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y);
+          };
+          const float bm = block_max();
+          if (j == 0) {
+            m_ref = bm;
+          } else if (__any_sync(0xffffffffu, bm > m_ref + 15.0f)) {  // some p would reach 2^15
+            const float m_new = fmaxf(m_ref, bm);
+            const float f = ex2_approx(m_ref - m_new);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t o[32];
+              tmem_ld32(tb + col_o + h * 32, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * f);
+              tmem_st32(tb + col_o + h * 32, o);
+            }
+            l_run *= f;
+            m_ref = m_new;
+          }
+          const float l_blk = exp_split(m_ref);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_full[t]);
+          l_run += l_blk;
+          continue;
+        }
         if (j == 0) m_ref = block_max();
         // One pass against the running reference m_ref (the max of block 0, or
         // of a later block that outgrew it).  Probabilities above 1 are fine:
-        // the final O / l is invariant to the reference, and f32 / bf16 hold
-        // p up to 2^127.  Only when a row's block sum passes 2^64 is the block
-        // redone against its own max, with O and l rescaled to match (O_t(j-1)
-        // is complete: S_t(j) was issued after it).
+        // the final O / l is invariant to the reference.  P is stored as f16
+        // (largest finite 65504), so when a row's block sum reaches 2^15 (every
+        // p of the row is then below it) the block is redone against its own
+        // max, with O and l rescaled to match (O_t(j-1) is complete: S_t(j)
+        // was issued after it).  Probabilities below the f16 range round to
+        // zero: at most 2^-24 each, against a row sum of at least 1.
         float l_blk = exp_pass(m_ref);
-        if (j > 0 && __any_sync(0xffffffffu, !(l_blk < 18446744073709551616.0f))) {  // TMEM access is warp-collective
+        if (j > 0 && __any_sync(0xffffffffu, !(l_blk < 32768.0f))) {  // TMEM access is warp-collective
           const float m_new = fmaxf(m_ref, block_max());
           const float f = ex2_approx(m_ref - m_new);
 #pragma unroll
@@ -361,10 +451,10 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   }
 }
 
-template <int OUT>
+template <int OUT, bool SPLIT>
 static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int images,
                                int heads, int tokens, void* out, __half* q8d, int* err, cudaStream_t s) {
-  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(k_attention_tc<OUT>), static_cast<int>(ATT_SMEM));
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(k_attention_tc<OUT, SPLIT>), static_cast<int>(ATT_SMEM));
   if (e != cudaSuccess) return e;
   // tile pairs share each K/V block; single tiles when pairs would not fill the SMs
   int tpi = 2;
@@ -381,10 +471,10 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
   la[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = la;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_attention_tc<OUT>, mq, mk, mv, heads, tokens, items, tpi, out, q8d, err);
+  return cudaLaunchKernelEx(&cfg, k_attention_tc<OUT, SPLIT>, mq, mk, mv, heads, tokens, items, tpi, out, q8d, err);
 }
 
-cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int images,
+cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* v, int images,
                            int heads, int tokens, int out_mode, void* out, __half* out_q8d, int* err,
                            cudaStream_t s) {
   if (images <= 0 || heads <= 0 || tokens <= 0) return cudaErrorInvalidValue;
@@ -393,13 +483,24 @@ cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const
   const void* bases[3] = {q, k, v};
   CUtensorMap* maps[3] = {&mq, &mk, &mv};
   for (int i = 0; i < 3; ++i)
-    if (!make_tmap_3d(maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, bases[i], 64, tokens, bh, 128,
+    if (!make_tmap_3d(maps[i], i == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, bases[i], 64, tokens, bh, 128,
                       static_cast<uint64_t>(tokens) * 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
+  // The split-P product for the Q8_0 output (its quantisation steps of
+  // about 1/127 amplify any error of O) and for the head-major f32 output of
+  // the operator API; the encoder's bf16 output takes it with VK_ATT_SPLIT=1.
+  static const bool split_bf16 = [] {
+    const char* e = getenv("VK_ATT_SPLIT");
+    return e != nullptr && e[0] == '1';
+  }();
   switch (out_mode) {
-    case ATTN_OUT_HEAD_F32: return launch_attn<ATTN_OUT_HEAD_F32>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
-    case ATTN_OUT_TOKEN_BF16: return launch_attn<ATTN_OUT_TOKEN_BF16>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
-    case ATTN_OUT_TOKEN_Q8: return launch_attn<ATTN_OUT_TOKEN_Q8>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
+    case ATTN_OUT_HEAD_F32:
+      return launch_attn<ATTN_OUT_HEAD_F32, true>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
+    case ATTN_OUT_TOKEN_BF16:
+      return split_bf16 ? launch_attn<ATTN_OUT_TOKEN_BF16, true>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s)
+                        : launch_attn<ATTN_OUT_TOKEN_BF16, false>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
+    case ATTN_OUT_TOKEN_Q8:
+      return launch_attn<ATTN_OUT_TOKEN_Q8, true>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
     default: return cudaErrorInvalidValue;
   }
 }

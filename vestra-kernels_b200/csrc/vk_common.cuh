@@ -309,6 +309,11 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
 __host__ __device__ constexpr uint32_t idesc_bf16_bmn(int M, int N) {
   return idesc_bf16(M, N) | (1u << 16);
 }
+// kind::f16 with f16 A/B (A and B of one MMA must share the type), f32 D,
+// A K-major and B MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16_bmn(int M, int N) {
+  return (1u << 4) | (1u << 16) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
 // Instruction descriptor: kind::i8 with signed A/B, s32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_s8(int M, int N) {
   return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
@@ -492,6 +497,10 @@ __device__ __forceinline__ float2 gelu_erf_ex2(float2 v) {
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 

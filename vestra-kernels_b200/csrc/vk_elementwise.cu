@@ -94,25 +94,29 @@ __global__ void __launch_bounds__(EW_THREADS)
   }
 }
 
-// Generic row length: one warp per row, three passes over global memory.
-__global__ void k_layernorm_generic(const float* __restrict__ x, float* y, int rows, int cols,
-                                    const float* __restrict__ g, const float* __restrict__ b, float eps) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= rows) return;
-  const float* xr = x + static_cast<size_t>(warp) * cols;
-  float s = 0.0f;
-  for (int c = lane; c < cols; c += 32) s += xr[c];
-  const float mean = warp_sum(s) / static_cast<float>(cols);
-  float q = 0.0f;
-  for (int c = lane; c < cols; c += 32) {
-    const float d = xr[c] - mean;
-    q += d * d;
+// f32 output (the reference's layernorm operator and f32 math): bit-exact
+// with scalar::layernorm (src/scalar.rs:83-114).  The row sum and the sum of
+// squared deviations are left folds over ascending columns from -0.0 (Rust's
+// f32 Sum), every product and sum separately rounded (no FMA contraction),
+// inv = 1 / sqrt with IEEE division and square root, then
+// (x - mean) * inv * g + b.  The fold is a serial chain per row, so one
+// thread owns one row; its 128-byte lines stay in L1 between the passes.
+__global__ void k_layernorm_exact(const float* __restrict__ x, float* y, int rows, int cols,
+                                  const float* __restrict__ g, const float* __restrict__ b, float eps) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const float* xr = x + static_cast<size_t>(row) * cols;
+  float s = -0.0f;
+  for (int c = 0; c < cols; ++c) s = __fadd_rn(s, xr[c]);
+  const float mean = __fdiv_rn(s, static_cast<float>(cols));
+  float q = -0.0f;
+  for (int c = 0; c < cols; ++c) {
+    const float d = __fsub_rn(xr[c], mean);
+    q = __fadd_rn(q, __fmul_rn(d, d));
   }
-  const float var = warp_sum(q) / static_cast<float>(cols);
-  const float inv = 1.0f / sqrtf(var + eps);
-  float* yr = y + static_cast<size_t>(warp) * cols;
-  for (int c = lane; c < cols; c += 32) yr[c] = (xr[c] - mean) * inv * g[c] + b[c];
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(q, static_cast<float>(cols)), eps)));
+  float* yr = y + static_cast<size_t>(row) * cols;
+  for (int c = 0; c < cols; ++c) yr[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[c], mean), inv), g[c]), b[c]);
 }
 
 cudaError_t layernorm_f32(const float* x, float* y, __nv_bfloat16* yb, int8_t* yq, __half* yd, int rows, int cols,
@@ -122,11 +126,12 @@ cudaError_t layernorm_f32(const float* x, float* y, __nv_bfloat16* yb, int8_t* y
   const bool vec_ok = (cols % 128 == 0) && cols <= 1024 &&
                       (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(g) % 16 == 0) &&
                       (reinterpret_cast<uintptr_t>(b) % 16 == 0);
-  if (!vec_ok) {
-    if (yb != nullptr || yq != nullptr || y == nullptr) return cudaErrorInvalidValue;
-    k_layernorm_generic<<<grid, EW_THREADS, 0, s>>>(x, y, rows, cols, g, b, eps);
+  if (y != nullptr) {  // f32 output: the bit-exact kernel (bf16 / Q8_0 outputs feed rounding anyway)
+    if (yb != nullptr || yq != nullptr) return cudaErrorInvalidValue;
+    k_layernorm_exact<<<(rows + 127) / 128, 128, 0, s>>>(x, y, rows, cols, g, b, eps);
     return cudaGetLastError();
   }
+  if (!vec_ok) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(EW_THREADS);
@@ -218,52 +223,62 @@ cudaError_t rope2d_f32(float* x, int heads, int n, int head_dim, const float* ro
   return cudaGetLastError();
 }
 
-// Fused Q/K LayerNorm (64-wide rows) + axial RoPE: one warp per row, lane l
-// holds dims l and l + 32; the rotation partner of dim d is d ^ 16.
+// Fused Q/K LayerNorm (64-wide rows) + axial RoPE, bit-exact with
+// normalize_and_rotate (src/specialized.rs:412-454): one thread per row, the
+// LayerNorm folds in ascending order as layernorm_row (src/scalar.rs:99-113),
+// then rotate_half on each 32-wide axis half (pair (i, i + 16)), every
+// product and sum separately rounded.
 __global__ void k_qk_norm_rope(float* q, float* k, int rows, int tokens, const float* __restrict__ qg,
                                const float* __restrict__ qb, const float* __restrict__ kg,
                                const float* __restrict__ kb, const float* __restrict__ rot, float eps) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= 2 * rows) return;
-  const bool is_k = warp >= rows;
-  const int row = is_k ? warp - rows : warp;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= 2 * rows) return;
+  const bool is_k = idx >= rows;
+  const int row = is_k ? idx - rows : idx;
   float* data = (is_k ? k : q) + static_cast<size_t>(row) * 64;
   const float* g = is_k ? kg : qg;
   const float* bt = is_k ? kb : qb;
-  float x0 = data[lane], x1 = data[lane + 32];
-  const float mean = warp_sum(x0 + x1) / 64.0f;
-  const float d0 = x0 - mean, d1 = x1 - mean;
-  const float var = warp_sum(d0 * d0 + d1 * d1) / 64.0f;
-  const float inv = 1.0f / sqrtf(var + eps);
-  x0 = __fadd_rn(__fmul_rn(__fmul_rn(d0, inv), g[lane]), bt[lane]);
-  x1 = __fadd_rn(__fmul_rn(__fmul_rn(d1, inv), g[lane + 32]), bt[lane + 32]);
-  const float p0 = __shfl_xor_sync(0xffffffffu, x0, 16);
-  const float p1 = __shfl_xor_sync(0xffffffffu, x1, 16);
-  const int token = row % tokens;
-  const int i = lane & 15;
-  const bool first = lane < 16;
-  // axis 0 for dims 0..31 (x0), axis 1 for dims 32..63 (x1)
-  const float* r0 = rot + (static_cast<size_t>(token) * 32 + i) * 2;
-  const float* r1 = rot + (static_cast<size_t>(token) * 32 + 16 + i) * 2;
-  const float s0 = r0[0], c0 = r0[1], s1 = r1[0], c1 = r1[1];
-  float y0, y1;
-  if (first) {
-    y0 = __fsub_rn(__fmul_rn(x0, c0), __fmul_rn(p0, s0));
-    y1 = __fsub_rn(__fmul_rn(x1, c1), __fmul_rn(p1, s1));
-  } else {
-    y0 = __fadd_rn(__fmul_rn(x0, c0), __fmul_rn(p0, s0));
-    y1 = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(p1, s1));
+  float v[64];
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    const float4 f = reinterpret_cast<const float4*>(data)[c];
+    v[4 * c] = f.x; v[4 * c + 1] = f.y; v[4 * c + 2] = f.z; v[4 * c + 3] = f.w;
   }
-  data[lane] = y0;
-  data[lane + 32] = y1;
+  float s = -0.0f;
+#pragma unroll
+  for (int c = 0; c < 64; ++c) s = __fadd_rn(s, v[c]);
+  const float mean = __fdiv_rn(s, 64.0f);
+  float sq = -0.0f;
+#pragma unroll
+  for (int c = 0; c < 64; ++c) {
+    const float d = __fsub_rn(v[c], mean);
+    sq = __fadd_rn(sq, __fmul_rn(d, d));
+  }
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, 64.0f), eps)));
+#pragma unroll
+  for (int c = 0; c < 64; ++c) v[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c], mean), inv), g[c]), bt[c]);
+  const int token = row % tokens;
+#pragma unroll
+  for (int axis = 0; axis < 2; ++axis) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float* r = rot + (static_cast<size_t>(token) * 32 + axis * 16 + i) * 2;
+      const float sn = r[0], cs = r[1];
+      const float a = v[axis * 32 + i], bb = v[axis * 32 + i + 16];
+      v[axis * 32 + i] = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(bb, sn));
+      v[axis * 32 + i + 16] = __fadd_rn(__fmul_rn(bb, cs), __fmul_rn(a, sn));
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 16; ++c)
+    reinterpret_cast<float4*>(data)[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 }
 cudaError_t qk_norm_rope_f32(float* q, float* k, int heads, int tokens, const float* qg, const float* qb,
                              const float* kg, const float* kb, const float* rot, float eps, cudaStream_t s) {
   const int rows = heads * tokens;
   if (rows == 0) return cudaSuccess;
-  const int grid = (2 * rows * 32 + EW_THREADS - 1) / EW_THREADS;
-  k_qk_norm_rope<<<grid, EW_THREADS, 0, s>>>(q, k, rows, tokens, qg, qb, kg, kb, rot, eps);
+  const int grid = (2 * rows + 127) / 128;
+  k_qk_norm_rope<<<grid, 128, 0, s>>>(q, k, rows, tokens, qg, qb, kg, kb, rot, eps);
   return cudaGetLastError();
 }
 
@@ -356,6 +371,16 @@ __global__ void k_cast_bf16(const float* x, __nv_bfloat16* y, size_t n) {
 cudaError_t cast_f32_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
   k_cast_bf16<<<ew_grid(n), EW_THREADS, 0, s>>>(x, y, n);
+  return cudaGetLastError();
+}
+
+__global__ void k_cast_f16(const float* x, __half* y, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    y[i] = __float2half_rn(x[i]);
+}
+cudaError_t cast_f32_f16(const float* x, __half* y, size_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  k_cast_f16<<<ew_grid(n), EW_THREADS, 0, s>>>(x, y, n);
   return cudaGetLastError();
 }
 

@@ -36,7 +36,8 @@ int prepare_weight(size_t k, size_t n, const float* w_host, int math, float** w3
 namespace {
 
 struct Acts {
-  __nv_bfloat16 *ln16, *q16, *k16, *v16, *att16, *h16;
+  __nv_bfloat16 *ln16, *q16, *k16, *att16, *h16;
+  __half* v16;  // V is f16: attention's P V product runs in f16
   int8_t *lnq, *attq, *hq;
   __half *lnd, *attd, *hd;
   float *ln32, *q32, *k32, *v32, *att32, *tok32, *h32;
@@ -56,7 +57,7 @@ void layout_acts(Arena& ar, int math, size_t M, size_t E, size_t F, Acts& a) {
   }
   a.q16 = ar.get<__nv_bfloat16>(M * E);
   a.k16 = ar.get<__nv_bfloat16>(M * E);
-  a.v16 = ar.get<__nv_bfloat16>(M * E);
+  a.v16 = ar.get<__half>(M * E);
   if (math == VK_MATH_BF16) {
     a.ln16 = ar.get<__nv_bfloat16>(M * E);
     a.att16 = ar.get<__nv_bfloat16>(M * E);

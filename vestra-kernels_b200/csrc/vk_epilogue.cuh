@@ -27,6 +27,11 @@ __device__ __forceinline__ QkvPos qkv_pos(const GemmEpi& p, int row, int col0) {
   return q;
 }
 
+// The V third of a bf16 QKV output is stored as IEEE f16: attention runs
+// its P V product in f16 (P with a 10-bit mantissa), and one MMA takes A and
+// B of the same type.
+__device__ __forceinline__ bool qkv_is_v(const GemmEpi& p, int col0) { return col0 >= 2 * p.heads * 64; }
+
 // bias32 / scale32 point at the 32 bias / scale values of this chunk
 // (16-byte aligned, global or shared memory) or are null.
 template <int MODE, bool FAST_GELU = false>
@@ -79,10 +84,11 @@ __device__ __forceinline__ void epi_math(const GemmEpi& p, int row, int col0, fl
         const float4 sc = __ldg(r + static_cast<size_t>(i2) * rt);  // (sin, cos) of 2 i2, 2 i2 + 1
         const int i = 2 * i2;
         const float a0 = v[i], b0 = v[i + 16], a1 = v[i + 1], b1 = v[i + 17];
-        v[i] = a0 * sc.y - b0 * sc.x;
-        v[i + 16] = b0 * sc.y + a0 * sc.x;
-        v[i + 1] = a1 * sc.w - b1 * sc.z;
-        v[i + 17] = b1 * sc.w + a1 * sc.z;
+        // separately rounded products and sums, as rotate_half computes them
+        v[i] = __fsub_rn(__fmul_rn(a0, sc.y), __fmul_rn(b0, sc.x));
+        v[i + 16] = __fadd_rn(__fmul_rn(b0, sc.y), __fmul_rn(a0, sc.x));
+        v[i + 1] = __fsub_rn(__fmul_rn(a1, sc.w), __fmul_rn(b1, sc.z));
+        v[i + 17] = __fadd_rn(__fmul_rn(b1, sc.w), __fmul_rn(a1, sc.z));
       }
     }
   }
@@ -94,6 +100,13 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
   for (int j = 0; j < 4; ++j)
     d[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
                       pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+}
+__device__ __forceinline__ void store_f16x32(__half* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    d[j] = make_uint4(pack_f16x2(v[8 * j], v[8 * j + 1]), pack_f16x2(v[8 * j + 2], v[8 * j + 3]),
+                      pack_f16x2(v[8 * j + 4], v[8 * j + 5]), pack_f16x2(v[8 * j + 6], v[8 * j + 7]));
 }
 __device__ __forceinline__ void store_f32x32(float* dst, const float (&v)[32]) {
   float4* d = reinterpret_cast<float4*>(dst);
@@ -122,8 +135,12 @@ __device__ __forceinline__ void epi_direct(const GemmEpi& p, int row, int col0, 
     const QkvPos q = qkv_pos(p, row, col0);
     const size_t off = ((static_cast<size_t>(q.image) * p.heads + q.head) * p.tokens + q.t) * 64 + q.axis * 32;
     void* base = q.g == 0 ? p.q : (q.g == 1 ? p.k : p.v);
-    if constexpr (MODE == EPI_QKV_BF16)
-      store_bf16x32(static_cast<__nv_bfloat16*>(base) + off, v);
+    if constexpr (MODE == EPI_QKV_BF16) {
+      if (q.g == 2)
+        store_f16x32(static_cast<__half*>(base) + off, v);
+      else
+        store_bf16x32(static_cast<__nv_bfloat16*>(base) + off, v);
+    }
     else
       store_f32x32(static_cast<float*>(base) + off, v);
   } else if constexpr (MODE == EPI_Q8_GELU) {

@@ -61,8 +61,9 @@ struct Cfg {
 // Writes this thread's 32 values as row `lane` of a 32-row staging tile in
 // the TMA 128-byte (f32) or 64-byte (bf16) swizzle, so that the 16-byte
 // chunks of one store instruction spread over all banks.
+// f16 packs IEEE half instead of bf16 (the V third of the QKV output).
 template <bool F32>
-__device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const float (&v)[32]) {
+__device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const float (&v)[32], bool f16 = false) {
   if constexpr (F32) {
     uint8_t* row = buf + lane * 128;
 #pragma unroll
@@ -71,6 +72,14 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const float (&
           make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   } else {
     uint8_t* row = buf + lane * 64;
+    if (f16) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(row + ((j ^ ((lane >> 1) & 3)) << 4)) =
+            make_uint4(pack_f16x2(v[8 * j], v[8 * j + 1]), pack_f16x2(v[8 * j + 2], v[8 * j + 3]),
+                       pack_f16x2(v[8 * j + 4], v[8 * j + 5]), pack_f16x2(v[8 * j + 6], v[8 * j + 7]));
+      return;
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       *reinterpret_cast<uint4*>(row + ((j ^ ((lane >> 1) & 3)) << 4)) =
@@ -144,20 +153,23 @@ __device__ __forceinline__ void epilogue_part(const GemmEpi& epi, const CUtensor
           for (int d = 0; d < 64; ++d) v[d] += sbias[cp * 64 + d];
         const QkvPos q = qkv_pos(epi, row, col0);
         if (q.g < 2) {
+          // layernorm_row's arithmetic (src/scalar.rs:99-113): ascending folds
+          // from -0.0, every product and sum separately rounded
           const float* gm = epi.qkn + q.g * 128;  // gamma, then beta
-          float sum = 0.0f;
+          float sum = -0.0f;
 #pragma unroll
-          for (int d = 0; d < 64; ++d) sum += v[d];
-          const float mean = sum / 64.0f;
-          float sq = 0.0f;
+          for (int d = 0; d < 64; ++d) sum = __fadd_rn(sum, v[d]);
+          const float mean = __fdiv_rn(sum, 64.0f);
+          float sq = -0.0f;
 #pragma unroll
           for (int d = 0; d < 64; ++d) {
-            const float dv = v[d] - mean;
-            sq = fmaf(dv, dv, sq);
+            const float dv = __fsub_rn(v[d], mean);
+            sq = __fadd_rn(sq, __fmul_rn(dv, dv));
           }
-          const float inv = 1.0f / sqrtf(sq / 64.0f + epi.qkn_eps);
+          const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, 64.0f), epi.qkn_eps)));
 #pragma unroll
-          for (int d = 0; d < 64; ++d) v[d] = (v[d] - mean) * inv * __ldg(gm + d) + __ldg(gm + 64 + d);
+          for (int d = 0; d < 64; ++d)
+            v[d] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[d], mean), inv), __ldg(gm + d)), __ldg(gm + 64 + d));
         }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -166,7 +178,7 @@ __device__ __forceinline__ void epilogue_part(const GemmEpi& epi, const CUtensor
           if (direct) {
             if (row < M) epi_direct<MODE>(epi, row, col0 + 32 * h, N, half);
           } else {
-            stage_row<false>(stage + (2 * cp + h) * OUT_BUF, lane, half);
+            stage_row<false>(stage + (2 * cp + h) * OUT_BUF, lane, half, qkv_is_v(epi, col0));
             staged = true;
           }
         }
@@ -204,7 +216,7 @@ __device__ __forceinline__ void epilogue_part(const GemmEpi& epi, const CUtensor
       continue;
     }
     if constexpr (GROUPED) {
-      stage_row<F32>(stage + c * OUT_BUF, lane, v);
+      stage_row<F32>(stage + c * OUT_BUF, lane, v, MODE == EPI_QKV_BF16 && qkv_is_v(epi, col0));
       staged = true;
       continue;
     }

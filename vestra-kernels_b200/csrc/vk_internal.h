@@ -106,6 +106,7 @@ cudaError_t pack_blocks_q8_0(const int8_t* qs, const __half* d, size_t nblocks, 
 cudaError_t unpack_blocks_q8_0(const void* blocks, size_t nblocks, int8_t* qs, __half* d,
                                cudaStream_t s);
 cudaError_t cast_f32_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s);
+cudaError_t cast_f32_f16(const float* x, __half* y, size_t n, cudaStream_t s);
 // w [K, N] f32 (reference layout) -> wt [N, K] bf16 / f32.
 cudaError_t transpose_cast_bf16(const float* w, __nv_bfloat16* wt, int K, int N, cudaStream_t s);
 cudaError_t transpose_f32(const float* w, float* wt, int K, int N, cudaStream_t s);
@@ -116,7 +117,7 @@ cudaError_t hnd_to_token_f32(const float* x, float* y, int images, int heads, in
 // bf16 path: out either head-major bf16/f32 or token-major bf16 [images*tokens, heads*64].
 enum AttnOut : int { ATTN_OUT_HEAD_F32 = 0, ATTN_OUT_TOKEN_BF16 = 1, ATTN_OUT_TOKEN_Q8 = 2 };
 cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k,
-                           const __nv_bfloat16* v, int images, int heads, int tokens,
+                           const __half* v, int images, int heads, int tokens,
                            int out_mode, void* out, __half* out_q8d, int* err, cudaStream_t s);
 // f32 SIMT online attention for any head_dim <= 128 (head-major in and out).
 cudaError_t attention_f32(const float* q, const float* k, const float* v, int bh, int tokens,
