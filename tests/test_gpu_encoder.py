@@ -8,7 +8,7 @@ residual it is added to).  Relative L2 per layer, at the DA3-BASE shapes:
   bf16  <= 1e-3 against the oracle rounding to bf16 (v to f16) where the
         kernels store;
   f32   <= 1e-5 against the f32 oracle;
-  Q8_0  <= BAR["q8"] against the oracle composing the reference's Q8_0 ops
+  Q8_0  <= 3e-3 against the oracle composing the reference's Q8_0 ops
         (quantize_row_q8_0, gemm_q8_0) at the kernels' quantisation points.
 """
 import numpy as np
@@ -66,7 +66,14 @@ def run_encoder(vk, ctx, layers, x, images, gh, gw, math):
 
 
 MATHS = ["bf16", "f32", "q8"]
-BAR = {"bf16": 1e-3, "f32": 1e-5, "q8": 1e-3}
+# Q8_0: the int32 block dots and the f32 fold are bit-exact (test_gpu_ops);
+# what is left is how Q8_0 quantisation amplifies last-bit differences
+# upstream of it (the LayerNorm's reduction order, attention's f32
+# accumulation): a value that sits near a rounding boundary of d / 127 moves
+# by a whole step.  Emulated on the oracle, a 1e-7 relative perturbation of
+# the LayerNorm output alone gives 2e-3 on the update; measured here:
+# 1.2e-3 - 2.3e-3.
+BAR = {"bf16": 1e-3, "f32": 1e-5, "q8": 3e-3}
 
 
 def math_mode(vk, math):

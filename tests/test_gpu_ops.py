@@ -267,7 +267,7 @@ def test_flash_attention_bf16(vk, ctx, oracle_lib, tokens, heads):
         got = host(out).reshape(q.shape)
         err = rel_l2(got, oracle_lib.attention_naive(q, k, v))
         print(f"bf16 attention tokens={tokens} rel_l2={err:.3e}")
-        assert err < 1e-3
+        assert err < 2e-5  # P V as f16 P_hi + P_lo: about 22 bits of P
     finally:
         ctx.set_math(vk.MATH_F32)
 
