@@ -317,6 +317,31 @@ def test_rope2d_bit_exact(vk, ctx, oracle_lib):
     assert np.array_equal(host(t2).reshape(x2.shape), oracle_lib.rope2d(x2, pos2, 100.0))
 
 
+def test_rope2d_device_tables(vk, ctx, oracle_lib):
+    """Rotations are built on the device from device positions (no host
+    round trip): a 72-wide grid and a second frequency are bit-exact through
+    the cached lookup table; positions outside it (negative, >= 4096) take
+    double-precision sin / cos, within an ulp of the host's f32 functions;
+    changed positions at the same address are picked up."""
+    pos = oracle_lib.da3_positions(48, 72)
+    (x,) = rng_inputs(101, (2, 3457, 64))
+    for freq in (100.0, 10000.0):
+        t = dev(x)
+        vk.rope2d(t, 2, 3457, 64, dev(pos, torch.int64), freq, ctx=ctx)
+        assert np.array_equal(host(t).reshape(x.shape), oracle_lib.rope2d(x, pos, freq))
+    pd = dev(pos, torch.int64)
+    pd += 3  # same buffer, new contents
+    t = dev(x)
+    vk.rope2d(t, 2, 3457, 64, pd, 100.0, ctx=ctx)
+    assert np.array_equal(host(t).reshape(x.shape), oracle_lib.rope2d(x, pos + 3, 100.0))
+    far = np.array([[-5, 4096], [70000, 12], [4095, -1]], np.int64)
+    (x3,) = rng_inputs(102, (1, 3, 64))
+    t3 = dev(x3)
+    vk.rope2d(t3, 1, 3, 64, dev(far, torch.int64), 100.0, ctx=ctx)
+    ref = oracle_lib.rope2d(x3, far, 100.0)
+    assert np.abs(host(t3).reshape(x3.shape) - ref).max() <= 4e-7 * max(1.0, float(np.abs(x3).max())) * 4
+
+
 def test_qk_norm_rope(vk, ctx, oracle_lib):
     pos = oracle_lib.da3_positions(24, 36)
     q, k, g, b = rng_inputs(110, (12, 865, 64), (12, 865, 64), (64,), (64,))

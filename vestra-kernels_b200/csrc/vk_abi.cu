@@ -1,6 +1,7 @@
 // vk_abi.cu -- the C ABI (include/vestra_b200.h): contexts, the operator
 // entry points of the reference's public API, prepared linears.  The encoder
 // driver lives in vk_encoder.cu.
+#include <cstring>
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -86,6 +87,7 @@ extern "C" int vk_destroy(vk_ctx* ctx) {
   cudaStreamSynchronize(ctx->stream);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->d_err) cudaFree(ctx->d_err);
+  for (auto& l : ctx->rope_luts) cudaFree(l.lut);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
   return VK_OK;
@@ -149,18 +151,44 @@ void host_rotations(const int64_t* pos, size_t n, size_t head_dim, float freq, s
     }
 }
 
-static int upload_rotations_from_device_positions(vk_ctx* ctx, const int64_t* pos_dev, size_t n, size_t head_dim,
-                                                  float freq, float* rot_dev) {
-  std::vector<int64_t> pos(2 * n);
-  VK_TRY_CUDA(cudaMemcpyAsync(pos.data(), pos_dev, pos.size() * sizeof(int64_t), cudaMemcpyDeviceToHost, ctx->stream),
-              "positions download");
-  VK_TRY_CUDA(cudaStreamSynchronize(ctx->stream), "positions download");
-  std::vector<float> rot;
-  host_rotations(pos.data(), n, head_dim, freq, rot);
-  VK_TRY_CUDA(cudaMemcpyAsync(rot_dev, rot.data(), rot.size() * sizeof(float), cudaMemcpyHostToDevice, ctx->stream),
-              "rotation upload");
-  // the host vector goes out of scope: wait for the copy to finish
-  VK_TRY_CUDA(cudaStreamSynchronize(ctx->stream), "rotation upload");
+// Per-token rotations of device positions, built on the device without a
+// host round trip: the context keeps, per (head_dim, freq), a lookup table
+// of the host's f32 sin / cos for integer positions [0, 4096) (built and
+// uploaded once, on the first call), which the table kernel indexes.  Grid
+// coordinates of any DA3 image size fall in that range; a position outside
+// it takes sin / cos in double precision rounded to f32 (within an ulp of
+// the host's f32 functions).
+static int rotations_from_device_positions(vk_ctx* ctx, const int64_t* pos_dev, size_t n, size_t head_dim,
+                                           float freq, float* rot_dev) {
+  const size_t half = head_dim / 2, quarter = half / 2;
+  if (quarter > 32) return vk_fail(VK_UNSUPPORTED_SHAPE, "RoPE: head_dim %zu above 128", head_dim);
+  uint32_t fbits;
+  std::memcpy(&fbits, &freq, 4);
+  vk_ctx::RopeLut* hit = nullptr;
+  for (auto& l : ctx->rope_luts)
+    if (l.quarter == quarter && l.freq_bits == fbits) hit = &l;
+  if (hit == nullptr) {
+    vk_ctx::RopeLut l{};
+    l.quarter = quarter;
+    l.freq_bits = fbits;
+    std::vector<int64_t> pos(2 * VK_ROPE_LUT_POSITIONS);
+    for (int p = 0; p < VK_ROPE_LUT_POSITIONS; ++p) pos[2 * p] = pos[2 * p + 1] = p;
+    std::vector<float> rot;  // [p][axis][i][2]; the table keeps axis 0
+    host_rotations(pos.data(), VK_ROPE_LUT_POSITIONS, head_dim, freq, rot);
+    std::vector<float> lut(static_cast<size_t>(VK_ROPE_LUT_POSITIONS) * quarter * 2);
+    for (size_t p = 0; p < static_cast<size_t>(VK_ROPE_LUT_POSITIONS); ++p)
+      std::memcpy(&lut[p * quarter * 2], &rot[p * quarter * 4], quarter * 2 * sizeof(float));
+    for (size_t i = 0; i < quarter; ++i) l.inv[i] = powf(freq, -2.0f * static_cast<float>(i) / static_cast<float>(half));
+    VK_TRY_CUDA(cudaMalloc(&l.lut, lut.size() * sizeof(float)), "RoPE table");
+    VK_TRY_CUDA(cudaMemcpy(l.lut, lut.data(), lut.size() * sizeof(float), cudaMemcpyHostToDevice), "RoPE table");
+    ctx->rope_luts.push_back(l);
+    hit = &ctx->rope_luts.back();
+  }
+  RopeInv inv{};
+  for (size_t i = 0; i < quarter; ++i) inv.v[i] = hit->inv[i];
+  VK_TRY_CUDA(rope_rotations_device(pos_dev, static_cast<int>(n), static_cast<int>(quarter), inv, hit->lut, rot_dev,
+                                    ctx->stream),
+              "RoPE rotations");
   return VK_OK;
 }
 
@@ -302,7 +330,7 @@ extern "C" int vk_qk_norm_rope_f32_da3_base(vk_ctx* ctx, float* q, float* k, siz
     return vk_fail(VK_ERR_INVALID_ARGUMENT, "vk_qk_norm_rope_f32_da3_base: NULL buffer");
   VK_TRY(ctx_reserve(ctx, tokens * 64 * sizeof(float) + 256));
   float* rot = static_cast<float*>(ctx->ws);
-  VK_TRY(upload_rotations_from_device_positions(ctx, positions_yx, tokens, 64, frequency, rot));
+  VK_TRY(rotations_from_device_positions(ctx, positions_yx, tokens, 64, frequency, rot));
   return vk_cuda_status(qk_norm_rope_f32(q, k, (int)heads, (int)tokens, q_gamma, q_beta, k_gamma, k_beta, rot, epsilon,
                                          ctx->stream),
                         "vk_qk_norm_rope_f32_da3_base");
@@ -330,7 +358,7 @@ extern "C" int vk_rope2d(vk_ctx* ctx, float* x, size_t heads, size_t n, size_t h
   VK_TRY(vk_dims_fit("vk_rope2d", {heads, n, head_dim}));
   VK_TRY(ctx_reserve(ctx, n * head_dim * sizeof(float) + 256));
   float* rot = static_cast<float*>(ctx->ws);
-  VK_TRY(upload_rotations_from_device_positions(ctx, pos_yx, n, head_dim, freq, rot));
+  VK_TRY(rotations_from_device_positions(ctx, pos_yx, n, head_dim, freq, rot));
   return vk_cuda_status(rope2d_f32(x, (int)heads, (int)n, (int)head_dim, rot, ctx->stream), "vk_rope2d");
 }
 

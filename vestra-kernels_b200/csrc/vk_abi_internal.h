@@ -21,6 +21,16 @@ struct vk_ctx {
   int* d_err = nullptr;  // device error word written by bounded waits
   void* ws = nullptr;    // grow-only scratch for the f32-interface operators
   size_t ws_bytes = 0;
+  // Rotation lookup tables of the RoPE operators, one per (head_dim, freq):
+  // (sin, cos) of position * inv_freq[i] for integer positions [0, VK_ROPE_LUT_POSITIONS),
+  // computed once on the host with the reference's f32 calls.
+  struct RopeLut {
+    size_t quarter;
+    uint32_t freq_bits;
+    float inv[32];
+    float* lut;
+  };
+  std::vector<RopeLut> rope_luts;
 };
 
 // Sub-allocates a workspace in two passes: a sizing pass (base == nullptr)

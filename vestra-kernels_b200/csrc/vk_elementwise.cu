@@ -196,6 +196,35 @@ cudaError_t layerscale_f32(float* x, size_t rows, size_t cols, const float* g, c
 }
 
 // ---------------------------------------------------------------- RoPE
+__global__ void k_rope_rotations(const int64_t* __restrict__ pos, int n, int quarter, RopeInv inv,
+                                 const float* __restrict__ lut, float* rot) {
+  const int total = n * 2 * quarter;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const int i = idx % quarter, axis = (idx / quarter) & 1, t = idx / (2 * quarter);
+    const int64_t p = pos[2 * t + axis];
+    float sn, cs;
+    if (p >= 0 && p < VK_ROPE_LUT_POSITIONS) {
+      const float2 sc = reinterpret_cast<const float2*>(lut)[p * quarter + i];
+      sn = sc.x;
+      cs = sc.y;
+    } else {
+      const float ang = __fmul_rn(static_cast<float>(p), inv.v[i]);
+      double ds, dc;
+      sincos(static_cast<double>(ang), &ds, &dc);
+      sn = static_cast<float>(ds);
+      cs = static_cast<float>(dc);
+    }
+    reinterpret_cast<float2*>(rot)[idx] = make_float2(sn, cs);
+  }
+}
+cudaError_t rope_rotations_device(const int64_t* pos, int n, int quarter, RopeInv inv, const float* lut,
+                                  float* rot, cudaStream_t s) {
+  const size_t total = static_cast<size_t>(n) * 2 * quarter;
+  if (total == 0) return cudaSuccess;
+  k_rope_rotations<<<ew_grid(total), EW_THREADS, 0, s>>>(pos, n, quarter, inv, lut, rot);
+  return cudaGetLastError();
+}
+
 // One thread per rotation pair.  rot[(t * 2 * quarter + axis * quarter + i) * 2 + {0: sin, 1: cos}]
 // as in src/rope.rs:49-60.  Products and sums are separately rounded (no FMA
 // contraction), so the result is bit-identical to the reference's rotate_half.

@@ -93,6 +93,16 @@ cudaError_t add_f32(float* dst, const float* src, size_t n, cudaStream_t s);
 cudaError_t add_bias_rows_f32(float* x, size_t rows, size_t cols, const float* bias,
                               cudaStream_t s);
 cudaError_t layerscale_f32(float* x, size_t rows, size_t cols, const float* g, cudaStream_t s);
+// Per-token rotation table rot[(t * 2q + axis * q + i) * 2 + {sin, cos}] from
+// device positions pos[t, 2]: integer positions in [0, lut_positions) are
+// looked up in lut[(p * q + i) * 2 + {sin, cos}] (bit-identical to the host
+// table); others fall back to sin / cos in double precision rounded to f32.
+constexpr int VK_ROPE_LUT_POSITIONS = 4096;
+struct RopeInv {
+  float v[32];
+};
+cudaError_t rope_rotations_device(const int64_t* pos, int n, int quarter, RopeInv inv, const float* lut,
+                                  float* rot, cudaStream_t s);
 cudaError_t rope2d_f32(float* x, int heads, int n, int head_dim, const float* rot,
                        cudaStream_t s,
                        int period = 0);  // rows of `rot` (0: n); token p uses row p % period
