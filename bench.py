@@ -3,11 +3,15 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl vestra|reference]
                     [--math bf16|q8|f32] [--images 64] [--grid 24x36]
 
-A step is one 12-layer encoder forward over `--images` synthetic images per
-GPU (random-init weights W~N(0,0.02), b~N(0,0.01), LayerScale 1e-5; tokens
-~N(0,1)), through the C ABI (vk_encoder_forward).  Images are independent, so
-under torchrun every rank runs its own shard (weak scaling, no collective);
-time is the max over ranks of CUDA-event time around K steps.
+A step is one 12-layer encoder forward over a global batch of `--images`
+synthetic images (64 at 504x336; random-init weights
+W~N(0,0.02), b~N(0,0.01), LayerScale 1e-5; tokens ~N(0,1)), through the C ABI
+(vk_encoder_forward).  Images are independent, so under torchrun every rank
+runs its contiguous shard of the batch (strong scaling, no collective on the
+data path); time is the max over ranks of CUDA-event time around K steps.
+The line also carries the weak-scaling figure (64 images per GPU), the
+timed NCCL gather of the outputs to rank 0, and the rest of config 5's
+sweep (16 images at 1008x672, Q8_0 weights) at the same GPU count.
 
 `e2e` is the same metric through vk_encoder_forward_host_async: pinned host tokens
 in, host result out, copies pipelined with the compute inside the timed
@@ -82,12 +86,16 @@ class ClockSampler:
         self.device = device
         self.proc = None
         self.lines = []
+        self.active = False  # only samples taken inside a timed region count
+
+    def mark(self, active: bool):
+        self.active = active
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except Exception:
@@ -96,7 +104,8 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            if self.active:
+                self.lines.append(line.strip())
 
     def __exit__(self, *a):
         if self.proc:
@@ -175,7 +184,7 @@ def run_reference(args, rank, world):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"DA3-BASE 12-layer encoder, 1 image per step @ {gh}x{gw} patches "
                                f"({gh * gw + 1} tokens), random-init weights", "images_per_step": 1,
                    "tokens": gh * gw + 1, "parallelism": "cpu threads"},
@@ -302,89 +311,143 @@ def dpt_consumers(vk, ctx, B, gh, gw, reps=5):
     return res
 
 
-def run_vestra(args, rank, world, local_rank):
+def time_encoder(vk, ctx, math, total, gh, gw, steps, warmup, rank, world, clk=None):
+    """One configuration: `total` images sharded image-wise over the ranks
+    (image_shard), K timed steps of the device path and K of the host path.
+    Returns the rank-max device and e2e milliseconds plus what the line
+    reports about the step."""
     import torch
 
-    import vestra_kernels as vk
-    from vestra_kernels.sharding import max_over_ranks
+    from vestra_kernels.sharding import image_shard, max_over_ranks
 
-    torch.cuda.set_device(local_rank)
-    math = {"bf16": vk.MATH_BF16, "q8": vk.MATH_Q8_0, "f32": vk.MATH_F32}[args.math]
-    gh, gw = args.grid
     T = gh * gw + 1
-    B = args.images
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)  # a real stream: the encoder is graph-captured on it
-    ctx = vk.Context(local_rank, stream=stream)
-    if args.dpt_only:
-        if rank == 0:
-            print(json.dumps({"dpt_consumers": dpt_consumers(vk, ctx, B, gh, gw, reps=args.steps), "images": B}),
-                  flush=True)
-        return
+    first, B = image_shard(total, rank, world)
     enc = vk.Encoder(ctx, make_layers(0), math=math)
-    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    x = torch.randn(B, T, E, device="cuda", generator=g)
+    g = torch.Generator(device="cuda").manual_seed(1234)
+    x_all = torch.randn(total, T, E, device="cuda", generator=g)
+    x = x_all[first:first + B].contiguous()
+    del x_all
     out = torch.empty_like(x)
-
-    def step():
-        enc.forward(x, out, B, gh, gw)
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    ctx.synchronize()
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
+    for _ in range(warmup):
+        enc.forward(x, out, B, gh, gw)
+    ctx.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
-    with ClockSampler(local_rank) as clk:
-        start.record()
-        for _ in range(args.steps):
-            step()
-        stop.record()
-        barrier()
-    ctx.synchronize()
+    if clk is not None:
+        clk.mark(True)
+    start.record()
+    for _ in range(steps):
+        enc.forward(x, out, B, gh, gw)
+    stop.record()
+    barrier()
+    if clk is not None:
+        clk.mark(False)
     ms = start.elapsed_time(stop)
-    launches = enc.last_launches() * args.steps
+    launches = enc.last_launches() * steps
 
-    # end to end: pinned host buffers through the C ABI
+    # end to end: pinned host buffers through the C ABI.  Warm-up: every
+    # slot of the three-slot ring runs eager, then captured, then replayed,
+    # so no graph capture falls inside the timed region
     hin = x.cpu().pin_memory()
     hout = torch.empty_like(hin).pin_memory()
-    # warm-up: every slot of the three-slot ring runs eager, then captured,
-    # then replayed, so no graph capture falls inside the timed region
     enc.forward_host(hin, hout, B, gh, gw)
-    for _ in range(3 * max(args.warmup, 3)):
+    for _ in range(3 * warmup):
         enc.forward_host_async(hin, hout, B, gh, gw)
     ctx.synchronize()
     barrier()
+    if clk is not None:
+        clk.mark(True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         enc.forward_host_async(hin, hout, B, gh, gw)  # every step copies its tokens in and its result out
     e1.record()
     barrier()
+    if clk is not None:
+        clk.mark(False)
     e2e_ms = e0.elapsed_time(e1)
+    res = {"ms": max_over_ranks(ms), "e2e_ms": max_over_ranks(e2e_ms), "launches": launches, "enc": enc, "x": x,
+           "out": out, "B": B, "h2d": int(hin.numel() * 4), "d2h": int(hout.numel() * 4)}
+    res["value"] = total / (res["ms"] / 1e3 / steps)
+    res["e2e"] = total / (res["e2e_ms"] / 1e3 / steps)
+    return res
+
+
+def run_vestra(args, rank, world, local_rank):
+    import torch
+
+    import vestra_kernels as vk
+    from vestra_kernels.sharding import gather_images, max_over_ranks
+
+    torch.cuda.set_device(local_rank)
+    math = {"bf16": vk.MATH_BF16, "q8": vk.MATH_Q8_0, "f32": vk.MATH_F32}[args.math]
+    gh, gw = args.grid
+    T = gh * gw + 1
+    total = args.images
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)  # a real stream: the encoder is graph-captured on it
+    ctx = vk.Context(local_rank, stream=stream)
+    if args.dpt_only:
+        if rank == 0:
+            print(json.dumps({"dpt_consumers": dpt_consumers(vk, ctx, total, gh, gw, reps=args.steps),
+                              "images": total}), flush=True)
+        return
+
+    with ClockSampler(local_rank) as clk:
+        r = time_encoder(vk, ctx, math, total, gh, gw, args.steps, args.warmup, rank, world, clk)
+    B, x, out, enc = r["B"], r["x"], r["out"], r["enc"]
+    ms, value, e2e_value = r["ms"], r["value"], r["e2e"]
+
+    # the optional final gather of the outputs to rank 0 (NCCL), timed alone
+    gather = None
+    if world > 1:
+        for _ in range(2):
+            gather_images(out, total)
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(3):
+            gather_images(out, total)
+        torch.cuda.synchronize()
+        gms = max_over_ranks((time.perf_counter() - t0) / 3 * 1e3)
+        gather = {"ms": gms, "bytes": total * T * E * 4,
+                  "note": "all ranks' f32 outputs to rank 0 with NCCL all_gather, wall clock, outside `value`"}
+
+    # weak scaling beside the strong figure: 64 images on every GPU
+    weak = None
+    if world > 1 and not args.no_sweep:
+        w = time_encoder(vk, ctx, math, total * world, gh, gw, args.steps, args.warmup, rank, world)
+        weak = {"value": w["value"], "e2e": w["e2e"], "images_per_gpu": total, "global_batch": total * world}
+        del w
+
+    # the rest of BASELINE config 5's sweep, at the same GPU count
+    sweep = None
+    if not args.no_sweep and args.math == "bf16" and (gh, gw) == (24, 36) and total == 64:
+        sweep = {}
+        for name, m, n_img, sh, sw in (("16img_3457tok_bf16", vk.MATH_BF16, 16, 48, 72),
+                                       ("64img_865tok_q8_0", vk.MATH_Q8_0, 64, 24, 36),
+                                       ("16img_3457tok_q8_0", vk.MATH_Q8_0, 16, 48, 72)):
+            k = max(3, args.steps // 4)
+            w = time_encoder(vk, ctx, m, n_img, sh, sw, k, args.warmup, rank, world)
+            sweep[name] = {"images_per_s": w["value"], "e2e_images_per_s": w["e2e"], "steps": k,
+                           "ms_per_step": w["ms"] / k, "tokens": sh * sw + 1, "global_batch": n_img,
+                           "whole_step_tflops": gflop_per_image(sh * sw + 1) * w["value"] / world / 1e3}
+            del w
 
     # per-kernel device time (eager forward with events between kernels)
     slots = enc.profile(x, out, B, gh, gw)
-
-    # the step before the encoder: patch embedding of the same batch (images
-    # [B, 3, 14 gh, 14 gw] -> tokens), timed on its own
     pe_ms = patch_embed_ms(vk, ctx, B, gh, gw, args.steps, math)
-    # the step after it: the DPT head's consumers of the encoder output
     dpt = dpt_consumers(vk, ctx, B, gh, gw) if not args.no_dpt else None
-
-    ms, e2e_ms = max_over_ranks(ms), max_over_ranks(e2e_ms)
     if rank != 0:
         return
 
     peaks = load_peaks()
-    images = B * world
-    value = images / (ms / 1e3 / args.steps)
-    e2e_value = images / (e2e_ms / 1e3 / args.steps)
     gf = gflop_per_image(T)
     # dominant kernel: the projection GEMM (slots 1, 3, 5, 6 of each block)
     proj_flop = 2.0 * B * T * E * (3 * E + E + F + F) * LAYERS
@@ -396,16 +459,17 @@ def run_vestra(args, rank, world, local_rank):
     total_ms_eager = sum(slots)
     line = {
         "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": {"bf16": "bf16", "q8": "int8", "f32": "f32"}[args.math], "data": "synthetic",
-        "config": {"workload": f"DA3-BASE 12-layer ViT encoder, {B} images/GPU @ {gh * 14}x{gw * 14} "
-                               f"({T} tokens), random-init weights, tokens ~N(0,1)",
-                   "images_per_gpu": B, "global_batch": images, "tokens": T, "layers": LAYERS,
-                   "math": args.math, "parallelism": f"image-sharded x{world}, no collective",
+        "config": {"workload": f"DA3-BASE 12-layer ViT encoder, {total} images @ {gh * 14}x{gw * 14} "
+                               f"({T} tokens) sharded image-wise over {world} GPU(s), random-init weights, "
+                               f"tokens ~N(0,1)",
+                   "global_batch": total, "images_per_gpu": B, "tokens": T, "layers": LAYERS,
+                   "math": args.math, "parallelism": f"image-sharded x{world}, no collective on the data path",
                    "l2": l2_note(B, T)},
-        "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": int(hin.numel() * 4),
-                "d2h_bytes_per_step": int(hout.numel() * 4)},
-        "gpu_launches": launches,
+        "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": r["h2d"],
+                "d2h_bytes_per_step": r["d2h"]},
+        "gpu_launches": r["launches"],
         "roofline": {"bound": "tensor", "kernel": "k_gemm_bf16 (projection GEMMs)" if math == vk.MATH_BF16 else
                      ("k_gemm_q8" if math == vk.MATH_Q8_0 else "k_gemm_f32"),
                      "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s", "frac": gemm_tflops / peak,
@@ -413,18 +477,22 @@ def run_vestra(args, rank, world, local_rank):
                      "traffic": traffic_from_profiles() if math == vk.MATH_BF16 else None,
                      "whole_step_tflops": gf * value / world / 1e3,
                      "whole_step_frac": gf * value / world / 1e3 / peak,
+                     "whole_step_frac_of_burst": gf * value / world / 1e3 / peaks["bf16"],
                      "attention_tflops": attn_tflops,
                      "slot_ms": dict(zip(["ln1", "qkv", "attention", "proj", "ln2", "fc1", "fc2"]
                                          if math != vk.MATH_F32 else
                                          ["ln1", "qkv", "rope_q", "rope_k", "attention", "to_tokens", "proj",
-                                          "ln2", "fc1", "fc2"], [round(x, 4) for x in slots])),
+                                          "ln2", "fc1", "fc2"], [round(v, 4) for v in slots])),
                      "kernel_ms": {"layernorm": slots[0] + slots[4] if math != vk.MATH_F32 else slots[0] + slots[7],
                                    "gemm": gemm_ms, "attention": attn_ms, "eager_total": total_ms_eager}},
         "clocks": clk.summary(),
+        "gather": gather,
+        "weak_scaling": weak,
+        "sweep": sweep,
         "patch_embed": None if pe_ms is None else {
             "ms_per_step": round(pe_ms, 4), "images_per_s": B / (pe_ms / 1e3),
             "tflops": 2.0 * B * gh * gw * 588 * E / (pe_ms / 1e3) / 1e12,
-            "note": "patchify + 588->768 projection + cls/position assembly of the same batch, outside `value`"},
+            "note": "patchify + 588->768 projection + cls/position assembly of this GPU's shard, outside `value`"},
         "dpt_consumers": dpt,
     }
     if world == 1 and not args.no_cpu:
@@ -445,6 +513,7 @@ def main():
     ap.add_argument("--grid", default="24x36")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-dpt", action="store_true", help="skip the DPT-consumer timings")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the sweep and weak-scaling configurations")
     ap.add_argument("--dpt-only", action="store_true",
                     help="run only the DPT-consumer kernels on --images images (for profiling)")
     args = ap.parse_args()
