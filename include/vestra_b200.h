@@ -140,9 +140,12 @@ int vk_gemm_q8_0_block_dots(vk_ctx* ctx, size_t m, size_t n, size_t k,
  * context and unpacks the blocks into a fixed 8 MiB array inside the library
  * instead of a cudaMalloc'd workspace: (m + n) * k + (m + n) * (k / 32) * 2
  * bytes must fit (VK_UNSUPPORTED_SHAPE otherwise).  The first call on a
- * device looks the array up and should come before any stream capture; calls
+ * device loads the module and should come before any stream capture; calls
  * that overlap on the GPU share the array and race.  `stream` is a
- * cudaStream_t (NULL = legacy default stream); a_q, b_q, c as in vk_gemm_q8_0. */
+ * cudaStream_t of the current device (NULL = legacy default stream;
+ * another device's stream is VK_ERR_INVALID_ARGUMENT); a_q, b_q, c as in
+ * vk_gemm_q8_0.  Device-side wait timeouts are not reported (there is no
+ * context to carry them): c may then be partly written. */
 int vk_gemm_q8_0_noalloc(void* stream, size_t m, size_t n, size_t k, const vk_block_q8_0* a_q,
                          const vk_block_q8_0* b_q, float* c);
 

@@ -218,7 +218,8 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       float m_ref = -INFINITY;
       float l_run = 0.0f;
       for (int j = 0; j < nb; ++j, ++sp) {
-        if (!mbar_wait(&s_full[t], sp & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+        // warp-uniform outcome: the TMEM reads after the wait are warp-collective
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], sp & 1, err, VK_DEV_TIMEOUT_EPILOGUE))) {
           ok = false;
           break;
         }
@@ -384,7 +385,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         if (lane == 0) mbar_arrive(&p_full[t]);
         l_run += l_blk;
       }
-      if (!ok || !mbar_wait(&o_done[t], ct & 1, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+      if (!ok || !__all_sync(0xffffffffu, mbar_wait(&o_done[t], ct & 1, err, VK_DEV_TIMEOUT_EPILOGUE))) {
         ok = false;
         break;
       }

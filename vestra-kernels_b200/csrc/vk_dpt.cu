@@ -516,7 +516,7 @@ __global__ void __launch_bounds__(IG_THREADS)
     const int r = q * 32 + lane;
     const int y = y0 + r / IG_BX, x = x0 + r % IG_BX;
     const bool inside = y < H && x < W;
-    if (mbar_wait(done, 0, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+    if (__all_sync(0xffffffffu, mbar_wait(done, 0, err, VK_DEV_TIMEOUT_EPILOGUE))) {  // TMEM reads are warp-collective
       tc_fence_after();
       float* o = out + ((static_cast<size_t>(img) * out_c + n0) * H + y) * W + x;
       const size_t plane = static_cast<size_t>(H) * W;

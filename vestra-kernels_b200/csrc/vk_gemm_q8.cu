@@ -176,7 +176,8 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
         if (b + 1 < nb) da_next = __half2float(__ldg(arow + b + 1));
         const uint32_t buf = blk % QNACC;
         const uint32_t bph = (blk / QNACC) & 1u;
-        if (!mbar_wait(&tfull[buf], bph, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+        // warp-uniform outcome: the TMEM read after the wait is warp-collective
+        if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], bph, err, VK_DEV_TIMEOUT_EPILOGUE))) {
           ok = false;
           break;
         }

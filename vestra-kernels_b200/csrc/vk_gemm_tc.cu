@@ -388,7 +388,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t aphase = (it >> 1) & 1;
       const int m0 = (tile / n_tiles) * C::TILE_M;
       const int n0 = (tile % n_tiles) * C::TILE_N;
-      if (!mbar_wait(&tfull[acc], aphase, err, VK_DEV_TIMEOUT_EPILOGUE)) {
+      // warp-uniform outcome: the TMEM reads after the wait are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aphase, err, VK_DEV_TIMEOUT_EPILOGUE))) {
         ok = false;  // every epilogue warp gives up at the same tile
         break;
       }

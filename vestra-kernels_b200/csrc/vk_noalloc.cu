@@ -16,48 +16,40 @@
 //    (each section rounded up to 256 bytes); larger problems are rejected
 //    with VK_UNSUPPORTED_SHAPE and a message;
 //  - every GPU that loads the library holds the 8 MiB until the process exits;
-//  - the first call on a device looks up the array's device address with
-//    cudaGetSymbolAddress (with that device current); make that first call
-//    before any stream capture;
+//  - every call looks up the array's device address on the current device
+//    with cudaGetSymbolAddress; make the first call on a device before any
+//    stream capture (it loads the module);
+//  - the stream must belong to the current device (VK_ERR_INVALID_ARGUMENT
+//    otherwise);
 //  - all calls share the one array: calls whose work overlaps on the GPU (on
 //    different streams without ordering) race on it;
 //  - the array keeps the last call's contents; each call overwrites every byte
 //    it reads before reading it, so nothing needs clearing;
 //  - device-side wait timeouts are not reported by this entry point (it has
-//    no context to carry an error word).
-#include <mutex>
-
+//    no context to carry an error word): a kernel that gave up a bounded wait
+//    leaves c partly written and the call has already returned VK_OK.
 #include "vestra_b200.h"
 #include "vk_abi_internal.h"
 #include "vk_internal.h"
 
 #define VK_NOALLOC_SCRATCH_BYTES (8u << 20)
-#define VK_NOALLOC_MAX_DEVICES 64
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[VK_NOALLOC_SCRATCH_BYTES];
 
-// Device address of the scratch array on `device` (the current device).
-static uint8_t* scratch_address(int device, int* status) {
-  static std::mutex mu;
-  static uint8_t* addr[VK_NOALLOC_MAX_DEVICES] = {};
-  std::lock_guard<std::mutex> lock(mu);
-  if (device < 0 || device >= VK_NOALLOC_MAX_DEVICES) {
-    *status = vk_fail(VK_ERR_NO_DEVICE, "vk_gemm_q8_0_noalloc: device %d out of range", device);
+// Device address of the scratch array on the current device.  Looked up on
+// every call (cheap once the module is loaded), so a context that was reset
+// and re-created never hands out a stale address.
+static uint8_t* scratch_address(int* status) {
+  // In host code the array's name is only a stand-in; kernels need the
+  // device address, looked up with the device current.
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    *status = vk_cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol, "vk_gemm_q8_0_noalloc: scratch lookup");
     return nullptr;
   }
-  if (addr[device] == nullptr) {
-    // In host code the array's name is only a stand-in; kernels need the
-    // device address, looked up once per device with that device current.
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      *status = vk_cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol, "vk_gemm_q8_0_noalloc: scratch lookup");
-      return nullptr;
-    }
-    addr[device] = static_cast<uint8_t*>(p);
-  }
   *status = VK_OK;
-  return addr[device];
+  return static_cast<uint8_t*>(p);
 }
 
 extern "C" int vk_gemm_q8_0_noalloc(void* stream, size_t m, size_t n, size_t k, const vk_block_q8_0* a_q,
@@ -82,8 +74,16 @@ extern "C" int vk_gemm_q8_0_noalloc(void* stream, size_t m, size_t n, size_t k, 
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return vk_cuda_status(e, "vk_gemm_q8_0_noalloc");
+  if (stream != nullptr) {  // the stream must belong to the current device
+    int sdev = -1;
+    e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev);
+    if (e != cudaSuccess) return vk_cuda_status(e, "vk_gemm_q8_0_noalloc: stream device");
+    if (sdev != device)
+      return vk_fail(VK_ERR_INVALID_ARGUMENT,
+                     "vk_gemm_q8_0_noalloc: stream belongs to device %d, current device is %d", sdev, device);
+  }
   int st = VK_OK;
-  uint8_t* base = scratch_address(device, &st);
+  uint8_t* base = scratch_address(&st);
   if (base == nullptr) return st;
   int8_t* aq = reinterpret_cast<int8_t*>(base);
   int8_t* bq = reinterpret_cast<int8_t*>(base + a_q_bytes);
