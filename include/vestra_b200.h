@@ -72,7 +72,12 @@ const char* vk_version(void);
 /* ------------------------------------------- DA3-BASE specialised operators
  * Device pointers.  These replace the five `*_da3_base` functions of
  * src/lib.rs.  The reference gates them to 865 tokens; here any token count
- * >= 1 is accepted (the 3457-token configuration included). */
+ * >= 1 is accepted (the 3457-token configuration included).  Like the
+ * reference's functions they take the f32 weight on every call; under
+ * VK_MATH_BF16 / VK_MATH_Q8_0 that means a conversion of the weight per call.
+ * A caller that runs the same weight repeatedly prepares it once with
+ * vk_prepare_linear and calls vk_linear_run (the reference's prepared-value
+ * route, CudaLinearF32), which converts nothing per call. */
 
 /* src/lib.rs:52 qkv_f32_da3_base: input [tokens, 768], weight [768, 2304],
  * bias [2304] -> q, k, v [12, tokens, 64] head-major (bias added, no RoPE). */
