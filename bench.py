@@ -154,6 +154,35 @@ def cpu_reference_seconds_per_image(grid_h, grid_w, layers, reps: int = 1):
     return statistics.median(times)
 
 
+INT8_DENSE_SPEC_TOPS = 4500.0  # B200 dense int8, NVIDIA's spec sheet (the 9 POPS figure is with 2:4 sparsity)
+
+
+def int8_peak_tops():
+    """Dense int8 tensor throughput measured here: torch._int_mm (a cuBLASLt
+    int8 GEMM, 8192^3, 2 ops per multiply-add), best of 5 after warm-up.
+    A denominator only; None where the call is unavailable."""
+    import torch
+
+    try:
+        n = 8192
+        a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+        b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda").t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = None
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        return 2.0 * n ** 3 / (best / 1e3) / 1e12
+    except Exception:
+        return None
+
+
 def traffic_from_profiles():
     """DRAM bytes per launch of the projection GEMM from the committed ncu
     summary (profiles/gemm_bf16_encoder64.md, line `traffic_bytes_per_launch:`)."""
@@ -438,6 +467,14 @@ def run_vestra(args, rank, world, local_rank):
             sweep[name] = {"images_per_s": w["value"], "e2e_images_per_s": w["e2e"], "steps": k,
                            "ms_per_step": w["ms"] / k, "tokens": sh * sw + 1, "global_batch": n_img,
                            "whole_step_tflops": gflop_per_image(sh * sw + 1) * w["value"] / world / 1e3}
+            if m == vk.MATH_Q8_0:
+                if "int8_peak_tops" not in sweep:
+                    p8 = int8_peak_tops()
+                    sweep["int8_peak_tops"] = {"value": p8 if p8 is not None else INT8_DENSE_SPEC_TOPS,
+                                               "kind": "measured here (torch._int_mm 8192^3)" if p8 is not None
+                                               else "spec sheet, not measured"}
+                sweep[name]["whole_step_frac_of_int8"] = (sweep[name]["whole_step_tflops"]
+                                                          / sweep["int8_peak_tops"]["value"])
             del w
 
     # per-kernel device time (eager forward with events between kernels)
@@ -456,6 +493,13 @@ def run_vestra(args, rank, world, local_rank):
     gemm_tflops = proj_flop / (gemm_ms / 1e3) / 1e12
     attn_tflops = (4.0 * H * T * T * 64 * B * LAYERS) / (attn_ms / 1e3) / 1e12
     peak = peaks["bf16_sustained"]
+    peak_kind = f"bf16 dense sustained, {peaks['source']}"
+    if math == vk.MATH_Q8_0:  # the Q8_0 GEMMs run on the int8 tensor cores
+        measured = int8_peak_tops()
+        if measured is not None:
+            peak, peak_kind = measured, "int8 dense, measured here (torch._int_mm 8192^3, best of 5)"
+        else:
+            peak, peak_kind = INT8_DENSE_SPEC_TOPS, "int8 dense, spec sheet (not measured)"
     total_ms_eager = sum(slots)
     line = {
         "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
@@ -472,8 +516,9 @@ def run_vestra(args, rank, world, local_rank):
         "gpu_launches": r["launches"],
         "roofline": {"bound": "tensor", "kernel": "k_gemm_bf16 (projection GEMMs)" if math == vk.MATH_BF16 else
                      ("k_gemm_q8" if math == vk.MATH_Q8_0 else "k_gemm_f32"),
-                     "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s", "frac": gemm_tflops / peak,
-                     "peak_kind": f"bf16 dense sustained, {peaks['source']}",
+                     "achieved": gemm_tflops, "peak": peak,
+                     "unit": "TOPS" if math == vk.MATH_Q8_0 else "TFLOP/s", "frac": gemm_tflops / peak,
+                     "peak_kind": peak_kind,
                      "traffic": traffic_from_profiles() if math == vk.MATH_BF16 else None,
                      "whole_step_tflops": gf * value / world / 1e3,
                      "whole_step_frac": gf * value / world / 1e3 / peak,
