@@ -213,6 +213,8 @@ __global__ void __launch_bounds__(A_THREADS, 1)
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
       int bh, q0;
       if (t >= item_tiles(it, bh, q0)) continue;
+      if (it + static_cast<int>(gridDim.x) >= items && items <= VK_EARLY_LAUNCH_ROUNDS * static_cast<int>(gridDim.x))
+        grid_launch_dependents();
       const int qrow = q0 + t * AQ + quad * 32 + lane;
       const uint32_t col_o = COL_O + (ct & 1) * 64;
       float m_ref = -INFINITY;

@@ -55,6 +55,19 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 // its dependents early: measured, that made the chain slower.)  Without the
 // attribute the wait returns at once.
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel in the stream be scheduled once every CTA of this grid
+// has executed it (or exited).  The persistent kernels issue it when a CTA
+// starts its last unit of work, and only for small grids (a few rounds of
+// work per CTA, as with 8 images per GPU), so that the next kernel's CTAs
+// take the SMs of CTAs that finish early.  Measured on the 12-layer
+// forward: +2.2% at 8 images, -1.8% at 64 (where it is not issued).  Every
+// CTA of this grid is resident by the time the dependents launch, so they
+// cannot starve it; their griddepcontrol.wait still waits for this grid to
+// complete.
+constexpr int VK_EARLY_LAUNCH_ROUNDS = 4;
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

@@ -157,6 +157,9 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       const int m0 = (tile / n_tiles) * QBM, n0 = (tile % n_tiles) * QBN;
+      if (tile + static_cast<int>(gridDim.x) >= num_tiles &&
+          num_tiles <= VK_EARLY_LAUNCH_ROUNDS * static_cast<int>(gridDim.x))
+        grid_launch_dependents();
       const int row = m0 + quad * 32 + lane;
       // weight scales of this column tile, f32, [nb][QBN]
       epi_bar();

@@ -386,6 +386,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for (int tile = unit; tile < num_tiles && ok; tile += units, ++it) {
       const int acc = it & 1;
       const uint32_t aphase = (it >> 1) & 1;
+      if (tile + units >= num_tiles && num_tiles <= VK_EARLY_LAUNCH_ROUNDS * units) grid_launch_dependents();
       const int m0 = (tile / n_tiles) * C::TILE_M;
       const int n0 = (tile % n_tiles) * C::TILE_N;
       // warp-uniform outcome: the TMEM reads after the wait are warp-collective
