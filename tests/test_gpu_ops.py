@@ -257,7 +257,7 @@ def test_flash_attention_f32(vk, ctx, oracle_lib, tokens):
     assert d.mean() <= 5e-5 and d.max() <= 5e-4  # src/cuda.rs:1613-1648 bounds
 
 
-@pytest.mark.parametrize("tokens,heads", [(865, 12), (3457, 2), (64, 3), (65, 1), (1, 2)])
+@pytest.mark.parametrize("tokens,heads", [(865, 12), (865, 48), (3457, 2), (64, 3), (65, 1), (1, 2), (97, 301)])
 def test_flash_attention_bf16(vk, ctx, oracle_lib, tokens, heads):
     ctx.set_math(vk.MATH_BF16)
     try:
