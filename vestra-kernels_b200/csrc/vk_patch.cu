@@ -45,26 +45,32 @@ __global__ void k_patchify_f32(const float* __restrict__ image, float* __restric
 }
 
 // As k_patchify_f32 into bf16 rows of `kpad` >= C * p * p columns (the tail
-// zero), the A operand of the tensor-core GEMM.
+// zero), the A operand of the tensor-core GEMM.  Driven by the input: block
+// row blockIdx.y is one image row (b, c, y), read coalesced, one thread per
+// pixel; pixel x lands in patch x / p at column c p^2 + (y % p) p + x % p,
+// so each patch receives a contiguous run of p values.  The padding columns
+// are zeroed by k_patch_pad.
 __global__ void k_patchify_bf16(const float* __restrict__ image, __nv_bfloat16* __restrict__ patches, int images,
                                 int height, int width, int patch, int channels, int kpad) {
   const int gw = width / patch, gh = height / patch;
-  const int row_width = channels * patch * patch;
-  const size_t per_image = static_cast<size_t>(gh) * gw * kpad;
-  const size_t total = per_image * images;
+  const int x = blockIdx.x * blockDim.x + threadIdx.x;
+  const int rows = images * channels * height;
+  for (int rid = blockIdx.y; rid < rows; rid += gridDim.y) {
+    if (x >= width) continue;
+    const int y = rid % height, bc = rid / height, c = bc % channels, b = bc / channels;
+    const float v = image[static_cast<size_t>(rid) * width + x];
+    const int px = x / patch, sx = x - px * patch, gy = y / patch, sy = y - gy * patch;
+    const size_t prow = static_cast<size_t>(b) * gh * gw + static_cast<size_t>(gy) * gw + px;
+    patches[prow * kpad + (c * patch + sy) * patch + sx] = __float2bfloat16_rn(v);
+  }
+}
+__global__ void k_patch_pad(__nv_bfloat16* __restrict__ patches, size_t rows, int row_width, int kpad) {
+  const int pad = kpad - row_width;
+  const size_t total = rows * pad;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t b = i / per_image;
-    const size_t r = i - b * per_image;
-    const int p = static_cast<int>(r / kpad);
-    const int w = static_cast<int>(r - static_cast<size_t>(p) * kpad);
-    float v = 0.0f;
-    if (w < row_width) {
-      const int c = w / (patch * patch), s = w - c * patch * patch;
-      const int y = (p / gw) * patch + s / patch, x = (p % gw) * patch + s % patch;
-      v = image[((b * channels + c) * height + y) * width + x];
-    }
-    patches[i] = __float2bfloat16_rn(v);
+    const size_t r = i / pad;
+    patches[r * kpad + row_width + (i - r * pad)] = __float2bfloat16_rn(0.0f);
   }
 }
 
@@ -227,6 +233,8 @@ extern "C" int vk_patch_embed_forward(vk_ctx* ctx, const vk_patch_embed* pe, siz
                    height, width, pe->patch);
   if (reinterpret_cast<uintptr_t>(position_dev) % 16 != 0 || reinterpret_cast<uintptr_t>(tokens_dev) % 16 != 0)
     return vk_fail(VK_UNSUPPORTED_SHAPE, "vk_patch_embed_forward: position and tokens must be 16-byte aligned");
+  VK_TRY(vk_dims_fit("vk_patch_embed_forward", {images * pe->channels * height, width, images * (height / pe->patch) *
+                                                 (width / pe->patch)}));
   const size_t np = (height / pe->patch) * (width / pe->patch), E = pe->embed;
   const size_t rows = images * np;
   cudaStream_t s = ctx->stream;
@@ -255,9 +263,16 @@ extern "C" int vk_patch_embed_forward(vk_ctx* ctx, const vk_patch_embed* pe, siz
   } else {
     auto* a = ar.get<__nv_bfloat16>(rows * pe->kpad);
     float* proj = ar.get<float>(rows * E);
-    k_patchify_bf16<<<grid_for(rows * pe->kpad), PT_THREADS, 0, s>>>(images_dev, a, (int)images, (int)height,
-                                                                      (int)width, (int)pe->patch, (int)pe->channels,
-                                                                      (int)pe->kpad);
+    {
+      const int in_rows = static_cast<int>(images * pe->channels * height);
+      const dim3 grid(static_cast<unsigned>((width + PT_THREADS - 1) / PT_THREADS),
+                      static_cast<unsigned>(in_rows < 65535 ? in_rows : 65535));
+      k_patchify_bf16<<<grid, PT_THREADS, 0, s>>>(images_dev, a, (int)images, (int)height, (int)width, (int)pe->patch,
+                                                  (int)pe->channels, (int)pe->kpad);
+      const int row_width = static_cast<int>(pe->channels * pe->patch * pe->patch);
+      if (static_cast<int>(pe->kpad) > row_width)
+        k_patch_pad<<<grid_for(rows * (pe->kpad - row_width)), PT_THREADS, 0, s>>>(a, rows, row_width, (int)pe->kpad);
+    }
     VK_TRY_CUDA(cudaGetLastError(), "vk_patch_embed_forward: patchify");
     epi.out = proj;
     VK_TRY_CUDA(gemm_bf16_tc(a, pe->w_bf16, (int)rows, (int)E, (int)pe->kpad, EPI_F32, epi, ctx->d_err, s),
