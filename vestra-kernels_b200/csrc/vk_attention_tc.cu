@@ -479,7 +479,7 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
 
 cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* v, int images,
                            int heads, int tokens, int out_mode, void* out, __half* out_q8d, int* err,
-                           cudaStream_t s) {
+                           cudaStream_t s, bool precise) {
   if (images <= 0 || heads <= 0 || tokens <= 0) return cudaErrorInvalidValue;
   CUtensorMap mq, mk, mv;
   const uint64_t bh = static_cast<uint64_t>(images) * heads;
@@ -490,8 +490,9 @@ cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const
                       static_cast<uint64_t>(tokens) * 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
   // The split-P product for the Q8_0 output (its quantisation steps of
-  // about 1/127 amplify any error of O) and for the head-major f32 output of
-  // the operator API; the encoder's bf16 output takes it with VK_ATT_SPLIT=1.
+  // about 1/127 amplify any error of O), for the head-major f32 output of the
+  // operator API, and for the encoder's bf16 output when the caller asks
+  // (`precise`: layers with Q/K LayerNorm) or with VK_ATT_SPLIT=1.
   static const bool split_bf16 = [] {
     const char* e = getenv("VK_ATT_SPLIT");
     return e != nullptr && e[0] == '1';
@@ -500,7 +501,7 @@ cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const
     case ATTN_OUT_HEAD_F32:
       return launch_attn<ATTN_OUT_HEAD_F32, true>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
     case ATTN_OUT_TOKEN_BF16:
-      return split_bf16 ? launch_attn<ATTN_OUT_TOKEN_BF16, true>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s)
+      return split_bf16 || precise ? launch_attn<ATTN_OUT_TOKEN_BF16, true>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s)
                         : launch_attn<ATTN_OUT_TOKEN_BF16, false>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
     case ATTN_OUT_TOKEN_Q8:
       return launch_attn<ATTN_OUT_TOKEN_Q8, true>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);

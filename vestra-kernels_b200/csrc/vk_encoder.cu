@@ -196,7 +196,11 @@ int encoder_enqueue(vk_encoder* enc, int* d_err, size_t images, size_t T, const 
       fc1.out = a.h16;
       VK_L(layernorm_f32(x, nullptr, a.ln16, nullptr, nullptr, M, E, L.ln1_g, L.ln1_b, eps, s));
       VK_L(gemm_bf16_tc(a.ln16, L.qkv_w16, M, 3 * E, E, EPI_QKV_BF16, qkv, d_err, s));
-      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)ai, H, (int)aT, ATTN_OUT_TOKEN_BF16, a.att16, nullptr, d_err, s));
+      // Q/K-normalised heads (DA3's late blocks) give unit-variance q and k,
+      // so sharper softmax rows whose f16 P rounding shows more in the
+      // update: those layers take the split P V product
+      VK_L(attention_bf16(a.q16, a.k16, a.v16, (int)ai, H, (int)aT, ATTN_OUT_TOKEN_BF16, a.att16, nullptr, d_err, s,
+                          L.qkn != nullptr));
       VK_L(gemm_bf16_tc(a.att16, L.proj_w16, M, E, E, EPI_RESID, proj, d_err, s));
       VK_L(layernorm_f32(x, nullptr, a.ln16, nullptr, nullptr, M, E, L.ln2_g, L.ln2_b, eps, s));
       VK_L(gemm_bf16_tc(a.ln16, L.fc1_w16, M, F, E, EPI_BF16_GELU, fc1, d_err, s));

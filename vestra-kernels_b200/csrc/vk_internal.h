@@ -128,7 +128,8 @@ cudaError_t hnd_to_token_f32(const float* x, float* y, int images, int heads, in
 enum AttnOut : int { ATTN_OUT_HEAD_F32 = 0, ATTN_OUT_TOKEN_BF16 = 1, ATTN_OUT_TOKEN_Q8 = 2 };
 cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k,
                            const __half* v, int images, int heads, int tokens,
-                           int out_mode, void* out, __half* out_q8d, int* err, cudaStream_t s);
+                           int out_mode, void* out, __half* out_q8d, int* err, cudaStream_t s,
+                           bool precise = false);
 // f32 SIMT online attention for any head_dim <= 128 (head-major in and out).
 cudaError_t attention_f32(const float* q, const float* k, const float* v, int bh, int tokens,
                           int head_dim, float* out, cudaStream_t s);
