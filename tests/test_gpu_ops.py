@@ -340,6 +340,12 @@ def test_rope2d_device_tables(vk, ctx, oracle_lib):
     vk.rope2d(t3, 1, 3, 64, dev(far, torch.int64), 100.0, ctx=ctx)
     ref = oracle_lib.rope2d(x3, far, 100.0)
     assert np.abs(host(t3).reshape(x3.shape) - ref).max() <= 4e-7 * max(1.0, float(np.abs(x3).max())) * 4
+    # head_dim above 128 (40 frequencies): the host-built table, bit-exact
+    pos4 = oracle_lib.da3_positions(3, 5)
+    (x4,) = rng_inputs(103, (2, 16, 160))
+    t4 = dev(x4)
+    vk.rope2d(t4, 2, 16, 160, dev(pos4, torch.int64), 100.0, ctx=ctx)
+    assert np.array_equal(host(t4).reshape(x4.shape), oracle_lib.rope2d(x4, pos4, 100.0))
 
 
 def test_qk_norm_rope(vk, ctx, oracle_lib):

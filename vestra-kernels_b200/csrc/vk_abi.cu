@@ -158,10 +158,26 @@ void host_rotations(const int64_t* pos, size_t n, size_t head_dim, float freq, s
 // coordinates of any DA3 image size fall in that range; a position outside
 // it takes sin / cos in double precision rounded to f32 (within an ulp of
 // the host's f32 functions).
+// head_dim above 128 (more than 32 frequencies): the positions are read back
+// and the table built on the host, with two synchronisations.
+static int rotations_via_host(vk_ctx* ctx, const int64_t* pos_dev, size_t n, size_t head_dim, float freq,
+                              float* rot_dev) {
+  std::vector<int64_t> pos(2 * n);
+  VK_TRY_CUDA(cudaMemcpyAsync(pos.data(), pos_dev, pos.size() * sizeof(int64_t), cudaMemcpyDeviceToHost, ctx->stream),
+              "positions download");
+  VK_TRY_CUDA(cudaStreamSynchronize(ctx->stream), "positions download");
+  std::vector<float> rot;
+  host_rotations(pos.data(), n, head_dim, freq, rot);
+  VK_TRY_CUDA(cudaMemcpyAsync(rot_dev, rot.data(), rot.size() * sizeof(float), cudaMemcpyHostToDevice, ctx->stream),
+              "rotation upload");
+  VK_TRY_CUDA(cudaStreamSynchronize(ctx->stream), "rotation upload");  // the host vector goes out of scope
+  return VK_OK;
+}
+
 static int rotations_from_device_positions(vk_ctx* ctx, const int64_t* pos_dev, size_t n, size_t head_dim,
                                            float freq, float* rot_dev) {
   const size_t half = head_dim / 2, quarter = half / 2;
-  if (quarter > 32) return vk_fail(VK_UNSUPPORTED_SHAPE, "RoPE: head_dim %zu above 128", head_dim);
+  if (quarter > 32) return rotations_via_host(ctx, pos_dev, n, head_dim, freq, rot_dev);
   uint32_t fbits;
   std::memcpy(&fbits, &freq, 4);
   vk_ctx::RopeLut* hit = nullptr;
