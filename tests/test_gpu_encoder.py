@@ -232,6 +232,25 @@ def test_large_batch_matches_single_images(vk, ctx, oracle_lib):
         assert err < 1e-3, (i, err)
 
 
+def test_eight_images_wide_residual_tiles(vk, ctx, oracle_lib):
+    """8 images (M = 6,920 rows, a GPU's shard at 8-way strong scaling): the
+    out-proj and fc2 GEMMs take 256 x 384 CTA-pair tiles (one round on 74 SM
+    pairs).  Every image against the same image run alone, and image 0's
+    update against the oracle."""
+    gh, gw = 24, 36
+    T = gh * gw + 1
+    layers = make_layers(1, 17, ls=1.0)
+    x = np.random.default_rng(18).standard_normal((8, T, E)).astype(np.float32)
+    big, _ = run_encoder(vk, ctx, layers, x, 8, gh, gw, vk.MATH_BF16)
+    for i in (0, 3, 7):
+        one, _ = run_encoder(vk, ctx, layers, x[i:i + 1].copy(), 1, gh, gw, vk.MATH_BF16)
+        assert rel_l2(big[i] - x[i], one[0] - x[i]) < 1e-3, i
+    ref = oracle_lib.encoder(x[0], layers, gh, gw, bf16_points=True)
+    err = rel_l2(big[0] - x[0], ref - x[0])
+    print(f"8-image block (256 x 384 residual tiles) update rel_l2={err:.3e}")
+    assert err < 1e-3
+
+
 def oracle_views_layer(oracle_lib, views, layer, gh, gw, joint, bf):
     """One layer over a group of views: jointly (a global layer) or per view."""
     T = gh * gw + 1

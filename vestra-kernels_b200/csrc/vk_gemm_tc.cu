@@ -37,14 +37,24 @@ constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int GEMM_THREADS = 320;
 constexpr int SLAB_BYTES = 128 * BK * 2;  // one 128-row operand slab per stage
 
-template <int MODE, bool PAIR>
+// WIDE (CTA pairs, residual epilogue only): 256 x 384 tiles, each CTA
+// staging 192 rows of W (two 96-row boxes) and issuing two N = 192 MMAs per
+// K step into one
+// 384-column accumulator (no second buffer: TMEM holds 512 columns).  For
+// the N = 768 GEMMs when their 256 x 256 tiles would need a second, mostly
+// idle round while 256 x 384 ones fit in one (a few images per GPU).
+template <int MODE, bool PAIR, bool WIDE = false>
 struct Cfg {
   static constexpr bool F32OUT = (MODE == EPI_F32 || MODE == EPI_RESID || MODE == EPI_QKV_F32);
   static constexpr int TILE_M = PAIR ? 256 : 128;  // rows of C per tile
-  static constexpr int TILE_N = PAIR ? 256 : 128;  // columns of C per tile
-  static constexpr int TMEM_COLS = 2 * TILE_N;
+  static constexpr int TILE_N = PAIR ? (WIDE ? 384 : 256) : 128;  // columns of C per tile
+  static constexpr int MMA_N = WIDE ? 192 : TILE_N;                // columns per MMA
+  static constexpr int B_ROWS = PAIR ? TILE_N / 2 : TILE_N;        // rows of W this CTA stages
+  static constexpr int B_SLAB = B_ROWS * BK * 2;
+  static constexpr int ACCS = WIDE ? 1 : 2;                        // TMEM accumulators
+  static constexpr int TMEM_COLS = WIDE ? 512 : 2 * TILE_N;
   static constexpr int WARP_COLS = TILE_N / 2;     // columns one epilogue warp handles
-  static constexpr int STAGE_BYTES = 2 * SLAB_BYTES;
+  static constexpr int STAGE_BYTES = SLAB_BYTES + B_SLAB;
   static constexpr int OUT_BUF = F32OUT ? 4096 : 2048;  // 32 x 32 staging tile
   // f32 outputs: two 32 x 32 tiles per warp, double buffered chunk by chunk;
   // bf16 outputs: the warp's whole 32 x WARP_COLS slice, one fence per tile
@@ -245,12 +255,12 @@ __device__ __forceinline__ void epilogue_part(const GemmEpi& epi, const CUtensor
   }
 }
 
-template <int MODE, bool PAIR>
+template <int MODE, bool PAIR, bool WIDE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmO0, const __grid_constant__ CUtensorMap tmO1,
                 const __grid_constant__ CUtensorMap tmO2, const GemmEpi epi, int M, int N, int K, int* err) {
-  using C = Cfg<MODE, PAIR>;
+  using C = Cfg<MODE, PAIR, WIDE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -309,7 +319,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       for (int tile = unit; tile < num_tiles && ok; tile += units) {
         const int m0 = (tile / n_tiles) * C::TILE_M + 128 * static_cast<int>(rank);
-        const int n0 = (tile % n_tiles) * C::TILE_N + 128 * static_cast<int>(rank);
+        // A CTA pair's MMA takes half of its N columns from each CTA's W
+        // rows: 128 + 128 for 256-wide tiles; for WIDE tiles each of the two
+        // N = 192 MMAs takes 96 + 96, so a CTA stages rows [96 rank, +96) and
+        // [192 + 96 rank, +96) of the tile's 384.
+        const int n0 = (tile % n_tiles) * C::TILE_N + (WIDE ? 96 : C::B_ROWS) * static_cast<int>(rank);
         for (int kb = 0; kb < kb_n; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, err, VK_DEV_TIMEOUT_PRODUCER)) {
             ok = false;
@@ -320,11 +334,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
             const uint32_t bar = mapa_shared(&full[stage], 0);
             tma_load_2d_cg2(sA + stage * SLAB_BYTES, &tmA, bar, kb * BK, m0);
-            tma_load_2d_cg2(sB + stage * SLAB_BYTES, &tmB, bar, kb * BK, n0);
+            tma_load_2d_cg2(sB + stage * C::B_SLAB, &tmB, bar, kb * BK, n0);
+            if constexpr (WIDE) tma_load_2d_cg2(sB + stage * C::B_SLAB + 96 * 128, &tmB, bar, kb * BK, n0 + 192);
           } else {
             mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
             tma_load_2d(sA + stage * SLAB_BYTES, &tmA, &full[stage], kb * BK, m0);
-            tma_load_2d(sB + stage * SLAB_BYTES, &tmB, &full[stage], kb * BK, n0);
+            tma_load_2d(sB + stage * C::B_SLAB, &tmB, &full[stage], kb * BK, n0);
           }
           if (++stage == C::STAGES) {
             stage = 0;
@@ -335,14 +350,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = idesc_bf16(C::TILE_M, C::TILE_N);
+      constexpr uint32_t idesc = idesc_bf16(C::TILE_M, C::MMA_N);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
       for (int tile = unit; tile < num_tiles && ok; tile += units, ++it) {
-        const int acc = it & 1;
-        const uint32_t aphase = (it >> 1) & 1;
+        const int acc = it % C::ACCS;
+        const uint32_t aphase = (it / C::ACCS) & 1;
         if (!mbar_wait(&tempty[acc], aphase ^ 1u, err, VK_DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::TILE_N);
@@ -353,16 +368,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
           tc_fence_after();
           const uint64_t adesc = smem_desc_k_sw128(smem_u32(sA + stage * SLAB_BYTES));
-          const uint64_t bdesc = smem_desc_k_sw128(smem_u32(sB + stage * SLAB_BYTES));
+          const uint64_t bdesc = smem_desc_k_sw128(smem_u32(sB + stage * C::B_SLAB));
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
-            if constexpr (PAIR)
+            if constexpr (PAIR) {
               umma_f16_cg2(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc + static_cast<uint64_t>(k * 2), idesc,
                            accum);
-            else
+              if constexpr (WIDE)  // columns [192, 384): W rows [96, 192) of each CTA's slab (12 KB on)
+                umma_f16_cg2(d_tmem + 192, adesc + static_cast<uint64_t>(k * 2),
+                             bdesc + static_cast<uint64_t>((96 * 128) >> 4) + static_cast<uint64_t>(k * 2), idesc,
+                             accum);
+            } else {
               umma_f16(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc + static_cast<uint64_t>(k * 2), idesc,
                        accum);
+            }
           }
           if constexpr (PAIR) umma_commit_cg2_mc(&empty[stage], 0x3); else umma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -384,8 +404,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     int it = 0;
     bool ok = true;
     for (int tile = unit; tile < num_tiles && ok; tile += units, ++it) {
-      const int acc = it & 1;
-      const uint32_t aphase = (it >> 1) & 1;
+      const int acc = it % C::ACCS;
+      const uint32_t aphase = (it / C::ACCS) & 1;
       if (tile + units >= num_tiles && num_tiles <= VK_EARLY_LAUNCH_ROUNDS * units) grid_launch_dependents();
       const int m0 = (tile / n_tiles) * C::TILE_M;
       const int n0 = (tile % n_tiles) * C::TILE_N;
@@ -431,12 +451,12 @@ struct OutMaps {
   CUtensorMap m[3];
 };
 
-template <int MODE, bool PAIR>
+template <int MODE, bool PAIR, bool WIDE = false>
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om, const GemmEpi& epi, int M, int N,
                    int K, int* err, cudaStream_t s) {
-  using C = Cfg<MODE, PAIR>;
+  using C = Cfg<MODE, PAIR, WIDE>;
   // CTAs (or CTA pairs) that can be resident at once, per device
-  int& max_units = *per_device_slot(reinterpret_cast<const void*>(k_gemm_bf16<MODE, PAIR>));
+  int& max_units = *per_device_slot(reinterpret_cast<const void*>(k_gemm_bf16<MODE, PAIR, WIDE>));
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(GEMM_THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
@@ -458,12 +478,12 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& 
   cfg.attrs = attr;
   cfg.numAttrs = na;
   if (max_units == 0) {
-    cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(k_gemm_bf16<MODE, PAIR>), static_cast<int>(C::SMEM));
+    cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(k_gemm_bf16<MODE, PAIR, WIDE>), static_cast<int>(C::SMEM));
     if (e != cudaSuccess) return e;
     int n = 0;
     if (PAIR) {
       cfg.gridDim = dim3(2 * (num_sms() / 2));
-      if (cudaOccupancyMaxActiveClusters(&n, k_gemm_bf16<MODE, PAIR>, &cfg) != cudaSuccess || n <= 0) n = num_sms() / 2;
+      if (cudaOccupancyMaxActiveClusters(&n, k_gemm_bf16<MODE, PAIR, WIDE>, &cfg) != cudaSuccess || n <= 0) n = num_sms() / 2;
     } else {
       n = num_sms();
     }
@@ -472,7 +492,7 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& 
   const int tiles = ((M + C::TILE_M - 1) / C::TILE_M) * (N / C::TILE_N);
   const int units = tiles < max_units ? tiles : max_units;
   cfg.gridDim = dim3(PAIR ? 2 * units : units);
-  return cudaLaunchKernelEx(&cfg, k_gemm_bf16<MODE, PAIR>, ta, tb, om.m[0], om.m[1], om.m[2], epi, M, N, K, err);
+  return cudaLaunchKernelEx(&cfg, k_gemm_bf16<MODE, PAIR, WIDE>, ta, tb, om.m[0], om.m[1], om.m[2], epi, M, N, K, err);
 }
 
 template <bool PAIR>
@@ -497,11 +517,17 @@ cudaError_t gemm_bf16_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, int M, 
   // CTA pairs (256 x 256 tiles) when they fill every SM pair at least once.
   static const bool pair_enabled = getenv("VK_GEMM_NO_PAIR") == nullptr;
   const bool pair = pair_enabled && (N % 256 == 0) && ((M + 255) / 256) * (N / 256) >= num_sms() / 2;
+  // residual GEMMs whose 256 x 256 tiles need a second, mostly idle round
+  // while 256 x 384 tiles fit in one
+  const int mt256 = (M + 255) / 256, pairs = num_sms() / 2;
+  static const bool wide_enabled = getenv("VK_GEMM_NO_WIDE") == nullptr;
+  const bool wide = pair_enabled && wide_enabled && mode == EPI_RESID && N % 384 == 0 && mt256 * (N / 384) <= pairs &&
+                    mt256 * (N / 256) > pairs;
   CUtensorMap ta, tb;
   if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, A, K, M, static_cast<uint64_t>(K) * 2, BK, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, W, K, N, static_cast<uint64_t>(K) * 2, BK, 128,
+  if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, W, K, N, static_cast<uint64_t>(K) * 2, BK, wide ? 96 : 128,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   OutMaps om;
@@ -524,6 +550,7 @@ cudaError_t gemm_bf16_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, int M, 
     ok = make_tmap_2d(&om.m[0], odt, epi.out, N, M, static_cast<uint64_t>(epi.ldo) * esz, 32, 32, oswz);
   }
   if (!ok) return cudaErrorInvalidValue;
+  if (wide) return launch<EPI_RESID, true, true>(ta, tb, om, epi, M, N, K, err, s);
   return pair ? dispatch<true>(mode, ta, tb, om, epi, M, N, K, err, s)
               : dispatch<false>(mode, ta, tb, om, epi, M, N, K, err, s);
 }
