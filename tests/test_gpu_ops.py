@@ -273,22 +273,27 @@ def test_flash_attention_bf16(vk, ctx, oracle_lib, tokens, heads):
 
 
 @pytest.mark.parametrize("boost", [1.0, 40.0, 400.0])
-def test_flash_attention_bf16_logit_jumps(vk, ctx, oracle_lib, boost):
-    """Keys in a late block whose logits exceed every earlier one by far (up
-    to ~3000 in score units): the online softmax must re-reference its
-    running maximum without overflowing."""
+@pytest.mark.parametrize("span", [(600, 610), (100, 105)])
+@pytest.mark.parametrize("split", ["1", "0"])
+def test_flash_attention_bf16_logit_jumps(vk, ctx, oracle_lib, boost, span, split, monkeypatch):
+    """Keys whose logits exceed every earlier one by far (up to ~3000 in
+    score units), in a late block or in block 0 past the 64 keys the first
+    reference is taken from: the online softmax must re-reference its
+    running maximum without overflowing.  Both kernels: split P (the
+    operator's) and single f16 P (the bf16 encoder's, VK_ATT_API_SPLIT=0)."""
+    monkeypatch.setenv("VK_ATT_API_SPLIT", split)
     ctx.set_math(vk.MATH_BF16)
     try:
         heads, tokens = 2, 865
         q, k, v = rng_inputs(91, *[(heads, tokens, 64)] * 3)
-        k[:, 600:610] *= np.float32(boost)
+        k[:, span[0]:span[1]] *= np.float32(boost)  # a late block, or block 0's second half
         q, k, v = (oracle_lib.round_bf16(t) for t in (q, k, v))
         out = torch.empty(q.size, device="cuda")
         assert vk.flash_attention_f32_da3_base(dev(q), dev(k), dev(v), heads, tokens, out, ctx=ctx)
         got = host(out).reshape(q.shape)
         assert np.isfinite(got).all()
         err = rel_l2(got, oracle_lib.attention_naive(q, k, v))
-        assert err < 1e-3, err
+        assert err < (2e-5 if split == "1" else 1e-3), err
     finally:
         ctx.set_math(vk.MATH_F32)
 

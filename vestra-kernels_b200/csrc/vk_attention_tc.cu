@@ -250,15 +250,34 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         };
         // p = 2^(s * log2e / 8 - m) packed as f16 pairs into pk; returns the row sum
         uint32_t pk[64];
-        auto exp_pass = [&](float m) -> float {
+        // set_ref (block 0): the reference m_ref is taken from the first 64
+        // keys, already in registers, instead of a separate max pass over S;
+        // keys past them may then give p above 1 (the 2^15 check below covers
+        // them).
+        auto exp_pass = [&](float m, bool set_ref) -> float {
           float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-          const float2 scale2 = make_float2(sl2, sl2), shift2 = make_float2(-m, -m);
+          float2 shift2 = make_float2(-m, -m);
+          const float2 scale2 = make_float2(sl2, sl2);
 #pragma unroll
           for (int c = 0; c < 4; c += 2) {
             uint32_t rr[64];
             tmem_ld32(tb + COL_S + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
             tmem_ld32(tb + COL_S + c * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
             tmem_wait_ld();
+            if (c == 0 && set_ref) {
+              float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+              if (full_block) {
+#pragma unroll
+                for (int i = 0; i < 64; i += 2)
+                  pm[(i >> 1) & 3] = max3f(pm[(i >> 1) & 3], __uint_as_float(rr[i]), __uint_as_float(rr[i + 1]));
+              } else {
+#pragma unroll
+                for (int i = 0; i < 64; ++i)
+                  if (i < valid) pm[i & 3] = fmaxf(pm[i & 3], __uint_as_float(rr[i]));
+              }
+              m_ref = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])) * sl2;
+              shift2 = make_float2(-m_ref, -m_ref);
+            }
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const int k0 = c * 32 + 2 * i;
@@ -352,7 +371,6 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           l_run += l_blk;
           continue;
         }
-        if (j == 0) m_ref = block_max();
         // One pass against the running reference m_ref (the max of block 0, or
         // of a later block that outgrew it).  Probabilities above 1 are fine:
         // the final O / l is invariant to the reference.  P is stored as f16
@@ -361,8 +379,10 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         // max, with O and l rescaled to match (O_t(j-1) is complete: S_t(j)
         // was issued after it).  Probabilities below the f16 range round to
         // zero: at most 2^-24 each, against a row sum of at least 1.
-        float l_blk = exp_pass(m_ref);
-        if (j > 0 && __any_sync(0xffffffffu, !(l_blk < 32768.0f))) {  // TMEM access is warp-collective
+        float l_blk = exp_pass(m_ref, j == 0);
+        // (in block 0 O holds nothing of this item yet: rescaling it is harmless,
+        // the item's first P V overwrites it)
+        if (__any_sync(0xffffffffu, !(l_blk < 32768.0f))) {  // TMEM access is warp-collective
           const float m_new = fmaxf(m_ref, block_max());
           const float f = ex2_approx(m_ref - m_new);
 #pragma unroll
@@ -376,7 +396,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           }
           l_run *= f;
           m_ref = m_new;
-          l_blk = exp_pass(m_ref);
+          l_blk = exp_pass(m_ref, false);
         }
         // P over the first 64 columns of S (S is no longer needed)
         tmem_st32(tb + COL_S, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
@@ -498,8 +518,14 @@ cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const
     return e != nullptr && e[0] == '1';
   }();
   switch (out_mode) {
-    case ATTN_OUT_HEAD_F32:
+    case ATTN_OUT_HEAD_F32: {
+      // VK_ATT_API_SPLIT=0 runs the operator on the single-f16-P kernel the
+      // bf16 encoder uses (read per call: the parity tests switch it)
+      const char* e = getenv("VK_ATT_API_SPLIT");
+      if (e != nullptr && e[0] == '0')
+        return launch_attn<ATTN_OUT_HEAD_F32, false>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
       return launch_attn<ATTN_OUT_HEAD_F32, true>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
+    }
     case ATTN_OUT_TOKEN_BF16:
       return split_bf16 || precise ? launch_attn<ATTN_OUT_TOKEN_BF16, true>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s)
                         : launch_attn<ATTN_OUT_TOKEN_BF16, false>(mq, mk, mv, images, heads, tokens, out, out_q8d, err, s);
