@@ -132,7 +132,7 @@ def test_patch_embed_f32_bit_exact(vk, ctx, oracle_lib):
     assert np.array_equal(host(out), ref)
 
 
-@pytest.mark.parametrize("images,h,w", [(3, 336, 504), (1, 28, 70)])
+@pytest.mark.parametrize("images,h,w", [(3, 336, 504), (1, 28, 70), (3, 98, 140), (5, 112, 168)])
 def test_patch_embed_bf16(vk, ctx, oracle_lib, images, h, w):
     imgs, wt, b, cls, pos, n = embedding_inputs(images, h, w, seed=images + h)
     pe = vk.PatchEmbed(ctx, wt, b, cls, channels=3, patch=14, math=vk.MATH_BF16)

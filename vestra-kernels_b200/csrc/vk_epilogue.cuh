@@ -70,6 +70,19 @@ __device__ __forceinline__ void epi_math(const GemmEpi& p, int row, int col0, fl
         v[j + 1] = gelu_erf(v[j + 1]);
       }
     }
+  } else if constexpr (MODE == EPI_TOKENS) {
+    // tokens = projected + position, the projection's (acc + bias) rounded
+    // first (vestra_prepend_cls_add_pos_f32, src/cuda.rs:321-334)
+    const int t = row % p.tokens;
+    const float4* ps = reinterpret_cast<const float4*>(p.pos + static_cast<size_t>(t + 1) * p.ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 q4 = __ldg(ps + j);
+      v[4 * j] += q4.x;
+      v[4 * j + 1] += q4.y;
+      v[4 * j + 2] += q4.z;
+      v[4 * j + 3] += q4.w;
+    }
   } else if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32) {
     const QkvPos q = qkv_pos(p, row, col0);
     if (p.rope != nullptr && q.g < 2) {
@@ -120,6 +133,9 @@ __device__ __forceinline__ void epi_direct(const GemmEpi& p, int row, int col0, 
     store_f32x32(static_cast<float*>(p.out) + row * p.ldo + col0, v);
   } else if constexpr (MODE == EPI_BF16 || MODE == EPI_BF16_GELU) {
     store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col0, v);
+  } else if constexpr (MODE == EPI_TOKENS) {
+    const int img = row / p.tokens, t = row - img * p.tokens;
+    store_f32x32(static_cast<float*>(p.out) + (static_cast<size_t>(img) * (p.tokens + 1) + 1 + t) * p.ldo + col0, v);
   } else if constexpr (MODE == EPI_RESID) {
     float4* dst = reinterpret_cast<float4*>(p.resid + row * p.ldo + col0);
 #pragma unroll

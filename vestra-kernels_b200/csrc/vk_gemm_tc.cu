@@ -45,7 +45,7 @@ constexpr int SLAB_BYTES = 128 * BK * 2;  // one 128-row operand slab per stage
 // idle round while 256 x 384 ones fit in one (a few images per GPU).
 template <int MODE, bool PAIR, bool WIDE = false>
 struct Cfg {
-  static constexpr bool F32OUT = (MODE == EPI_F32 || MODE == EPI_RESID || MODE == EPI_QKV_F32);
+  static constexpr bool F32OUT = (MODE == EPI_F32 || MODE == EPI_RESID || MODE == EPI_QKV_F32 || MODE == EPI_TOKENS);
   static constexpr int TILE_M = PAIR ? 256 : 128;  // rows of C per tile
   static constexpr int TILE_N = PAIR ? (WIDE ? 384 : 256) : 128;  // columns of C per tile
   static constexpr int MMA_N = WIDE ? 192 : TILE_N;                // columns per MMA
@@ -107,6 +107,8 @@ __device__ __forceinline__ void store_chunk(const GemmEpi& epi, const CUtensorMa
                                             int t0) {
   if constexpr (MODE == EPI_RESID) {
     tma_reduce_add_2d(tmO0, buf, col0, row0);
+  } else if constexpr (MODE == EPI_TOKENS) {
+    tma_store_3d(tmO0, buf, col0, t0, img);  // the map starts at token row 1 of image 0
   } else if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32) {
     const QkvPos q = qkv_pos(epi, row0, col0);
     const CUtensorMap* map = q.g == 0 ? tmO0 : (q.g == 1 ? tmO1 : tmO2);
@@ -124,14 +126,14 @@ __device__ __forceinline__ void epilogue_part(const GemmEpi& epi, const CUtensor
                                               const CUtensorMap* tmO2, int M, int N, int row0, int c0,
                                               uint32_t tbase, const float* sbias, const float* sscale,
                                               uint8_t* stage, int& sb, int lane, Release release) {
-  constexpr bool F32 = (MODE == EPI_F32 || MODE == EPI_RESID || MODE == EPI_QKV_F32);
+  constexpr bool F32 = (MODE == EPI_F32 || MODE == EPI_RESID || MODE == EPI_QKV_F32 || MODE == EPI_TOKENS);
   constexpr int OUT_BUF = F32 ? 4096 : 2048;
   const int row = row0 + lane;
   // A 32-row chunk of the head-major QKV output that crosses an image
   // boundary (or the end of M) is written row by row instead of by TMA.
   bool direct = false;
   int img = 0, t0 = 0;
-  if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32) {
+  if constexpr (MODE == EPI_QKV_BF16 || MODE == EPI_QKV_F32 || MODE == EPI_TOKENS) {
     img = row0 / epi.tokens;
     t0 = row0 - img * epi.tokens;
     direct = (t0 + 32 > epi.tokens) || (row0 + 32 > M);
@@ -505,6 +507,7 @@ cudaError_t dispatch(int mode, const CUtensorMap& ta, const CUtensorMap& tb, con
     case EPI_RESID: return launch<EPI_RESID, PAIR>(ta, tb, om, epi, M, N, K, err, s);
     case EPI_QKV_BF16: return launch<EPI_QKV_BF16, PAIR>(ta, tb, om, epi, M, N, K, err, s);
     case EPI_QKV_F32: return launch<EPI_QKV_F32, PAIR>(ta, tb, om, epi, M, N, K, err, s);
+    case EPI_TOKENS: return launch<EPI_TOKENS, PAIR>(ta, tb, om, epi, M, N, K, err, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -533,7 +536,7 @@ cudaError_t gemm_bf16_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, int M, 
   OutMaps om;
   memset(&om, 0, sizeof(om));
   bool ok = true;
-  const bool f32 = (mode == EPI_F32 || mode == EPI_RESID || mode == EPI_QKV_F32);
+  const bool f32 = (mode == EPI_F32 || mode == EPI_RESID || mode == EPI_QKV_F32 || mode == EPI_TOKENS);
   const CUtensorMapDataType odt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const uint64_t esz = f32 ? 4 : 2;
   const CUtensorMapSwizzle oswz = f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -544,6 +547,12 @@ cudaError_t gemm_bf16_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, int M, 
     for (int g = 0; g < 3 && ok; ++g)
       ok = make_tmap_3d(&om.m[g], odt, bases[g], 64, epi.tokens, images * epi.heads, 64 * esz,
                         static_cast<uint64_t>(epi.tokens) * 64 * esz, 32, 32, oswz);
+  } else if (mode == EPI_TOKENS) {
+    // [images][tokens + 1][N] f32 from token row 1: patch p of image b is row 1 + p
+    if (epi.tokens <= 0 || M % epi.tokens != 0 || epi.pos == nullptr || epi.ldo != N) return cudaErrorInvalidValue;
+    const uint64_t images = M / epi.tokens;
+    ok = make_tmap_3d(&om.m[0], odt, static_cast<float*>(epi.out) + N, N, epi.tokens, images,
+                      static_cast<uint64_t>(N) * esz, static_cast<uint64_t>(epi.tokens + 1) * N * esz, 32, 32, oswz);
   } else if (mode == EPI_RESID) {
     ok = make_tmap_2d(&om.m[0], odt, epi.resid, N, M, static_cast<uint64_t>(epi.ldo) * esz, 32, 32, oswz);
   } else {

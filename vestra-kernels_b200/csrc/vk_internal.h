@@ -22,6 +22,7 @@ enum EpiMode : int {
   EPI_QKV_F32 = 5,    // head-major f32 q/k/v, optional RoPE on q and k
   EPI_Q8_GELU = 6,    // Q8_0 blocks of gelu(acc + bias)          (fc1, Q8_0 mode)
   EPI_F32_GELU = 7,   // out_f32 = gelu(acc + bias)               (fc1, f32 mode)
+  EPI_TOKENS = 8,     // out_f32[img][1 + p] = (acc + bias) + pos[1 + p]   (patch embedding; rows are (img, p))
 };
 
 struct GemmEpi {
@@ -37,6 +38,7 @@ struct GemmEpi {
   int tokens = 0;                // rows per image (per group of views for a global layer)
   int rope_tokens = 0;           // rows of the rotation table (0: tokens); token t uses row t % rope_tokens
   int heads = 0;                 // embed = heads * 64
+  const float* pos = nullptr;    // [tokens + 1, ldo] position table (EPI_TOKENS; `tokens` = patches per image)
   const float* qkn = nullptr;    // [4][64] q gamma, q beta, k gamma, k beta: LayerNorm of each q / k head before RoPE, or null
   float qkn_eps = 0.0f;
   int8_t* q8 = nullptr;          // [M, N] int8 quants (EPI_Q8_GELU)

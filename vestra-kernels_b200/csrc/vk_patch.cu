@@ -74,6 +74,22 @@ __global__ void k_patch_pad(__nv_bfloat16* __restrict__ patches, size_t rows, in
   }
 }
 
+// tokens[b][0] = cls + position[0] for every image (the bf16 path, whose
+// GEMM epilogue writes the patch rows).
+__global__ void k_cls_rows(const float* __restrict__ cls, const float* __restrict__ position, float* __restrict__ tokens,
+                           int images, int patch_count, int embed) {
+  const int e4 = embed / 4;
+  const size_t total = static_cast<size_t>(images) * e4;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t b = i / e4;
+    const int c = static_cast<int>(i - b * e4);
+    const float4 v = reinterpret_cast<const float4*>(cls)[c], q = reinterpret_cast<const float4*>(position)[c];
+    reinterpret_cast<float4*>(tokens)[b * (static_cast<size_t>(patch_count) + 1) * e4 + c] =
+        make_float4(v.x + q.x, v.y + q.y, v.z + q.z, v.w + q.w);
+  }
+}
+
 // tokens[b][0] = cls + position[0]; tokens[b][t] = projected[b][t - 1] + position[t]
 // (value + position, as the reference kernel).  float4 per thread.
 __global__ void k_assemble_tokens(const float* __restrict__ projected, const float* __restrict__ cls,
@@ -239,11 +255,12 @@ extern "C" int vk_patch_embed_forward(vk_ctx* ctx, const vk_patch_embed* pe, siz
   const size_t rows = images * np;
   cudaStream_t s = ctx->stream;
   Arena sizing;
-  if (pe->math == VK_MATH_F32)
+  if (pe->math == VK_MATH_F32) {
     sizing.get<float>(rows * pe->k);
-  else
+    sizing.get<float>(rows * E);  // the projection, assembled into tokens after
+  } else {
     sizing.get<__nv_bfloat16>(rows * pe->kpad);
-  sizing.get<float>(rows * E);
+  }
   VK_TRY(ctx_reserve(ctx, sizing.off + 256));
   Arena ar{ctx->ws, 0};
   GemmEpi epi;
@@ -262,7 +279,6 @@ extern "C" int vk_patch_embed_forward(vk_ctx* ctx, const vk_patch_embed* pe, siz
                                                                                   (int)images, (int)np, (int)E);
   } else {
     auto* a = ar.get<__nv_bfloat16>(rows * pe->kpad);
-    float* proj = ar.get<float>(rows * E);
     {
       const int in_rows = static_cast<int>(images * pe->channels * height);
       const dim3 grid(static_cast<unsigned>((width + PT_THREADS - 1) / PT_THREADS),
@@ -274,11 +290,16 @@ extern "C" int vk_patch_embed_forward(vk_ctx* ctx, const vk_patch_embed* pe, siz
         k_patch_pad<<<grid_for(rows * (pe->kpad - row_width)), PT_THREADS, 0, s>>>(a, rows, row_width, (int)pe->kpad);
     }
     VK_TRY_CUDA(cudaGetLastError(), "vk_patch_embed_forward: patchify");
-    epi.out = proj;
-    VK_TRY_CUDA(gemm_bf16_tc(a, pe->w_bf16, (int)rows, (int)E, (int)pe->kpad, EPI_F32, epi, ctx->d_err, s),
+    // the GEMM's epilogue adds the positions and writes each patch straight
+    // to its token row (1 + p of its image); the cls rows come from a small
+    // kernel
+    epi.out = tokens_dev;
+    epi.tokens = static_cast<int>(np);
+    epi.pos = position_dev;
+    VK_TRY_CUDA(gemm_bf16_tc(a, pe->w_bf16, (int)rows, (int)E, (int)pe->kpad, EPI_TOKENS, epi, ctx->d_err, s),
                 "vk_patch_embed_forward: projection");
-    k_assemble_tokens<<<grid_for((np + 1) * (E / 4) * images), PT_THREADS, 0, s>>>(proj, pe->cls, position_dev, tokens_dev,
-                                                                                  (int)images, (int)np, (int)E);
+    k_cls_rows<<<grid_for(images * (E / 4)), PT_THREADS, 0, s>>>(pe->cls, position_dev, tokens_dev, (int)images,
+                                                                  (int)np, (int)E);
   }
   return vk_cuda_status(cudaGetLastError(), "vk_patch_embed_forward: assembly");
 }
