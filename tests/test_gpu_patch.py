@@ -159,6 +159,24 @@ def test_patch_embed_batch_equals_single_images(vk, ctx):
         assert np.array_equal(host(one)[0], host(whole)[i])
 
 
+def test_patch_embed_pair_tiles(vk, ctx, oracle_lib):
+    """8 images at 504x336 (6,912 patch rows): the projection runs on CTA-pair
+    tiles, its epilogue writing each patch at its token row.  Against the
+    single-image runs (single-CTA tiles) and the oracle for two images."""
+    h, w = 336, 504
+    imgs, wt, b, cls, pos, n = embedding_inputs(8, h, w, seed=11)
+    pe = vk.PatchEmbed(ctx, wt, b, cls, channels=3, patch=14, math=vk.MATH_BF16)
+    whole = torch.empty((8, n + 1, 768), device="cuda")
+    assert pe(dev(imgs), dev(pos), whole, 8, h, w)
+    got = host(whole)
+    for i in (0, 5, 7):
+        one = torch.empty((1, n + 1, 768), device="cuda")
+        assert pe(dev(imgs[i:i + 1]), dev(pos), one, 1, h, w)
+        assert rel_l2(host(one)[0], got[i]) < 1e-6, i
+    ref = reference_embedding(oracle_lib, imgs[6:8], wt, b, cls, pos, 14, round_bf16=True)
+    assert rel_l2(got[6:8], ref) < 1e-3
+
+
 def test_patch_embed_rejects_non_multiple_grid(vk, ctx):
     imgs, wt, b, cls, pos, n = embedding_inputs(1, 28, 28)
     pe = vk.PatchEmbed(ctx, wt, b, cls, channels=3, patch=14, math=vk.MATH_BF16)
