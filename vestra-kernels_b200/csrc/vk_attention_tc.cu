@@ -9,6 +9,9 @@
 // tiles) items.  Every K/V block is loaded once for the item's two tiles,
 // and the tiles ping-pong on the tensor core: while the softmax warps of one
 // work on S_t(j), the tensor core runs the other tile's O += P V and next S.
+// When a head has an odd number of query tiles (865 tokens: 7), the heads'
+// last tiles are paired across heads instead of running alone: such an item
+// streams two K/V sequences, one per tile.
 // The Q tiles and the O accumulators are double-buffered across items, so
 // the next item's loads and first MMAs overlap this item's output.
 //
@@ -59,8 +62,8 @@ constexpr size_t ATT_SMEM = 1024 + TILE_BYTES * (4 + 2 * AST) + 512;
 template <int OUT, bool SPLIT>
 __global__ void __launch_bounds__(A_THREADS, 1)
     k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, int heads, int tokens, int items, int tpi, void* out,
-                   __half* out_q8d, int* err) {
+                   const __grid_constant__ CUtensorMap tmV, int heads, int tokens, int items, int tpi, int rph,
+                   int mixed_from, int bh_count, void* out, __half* out_q8d, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;  // [item parity][tile]
@@ -78,14 +81,38 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // An item is `tpi` (2, or 1 when pairs would leave SMs idle) query tiles
-  // of one (image, head).
-  const int pairs = (tokens + tpi * AQ - 1) / (tpi * AQ);  // items per (image, head)
+  // Items [0, mixed_from) are `tpi` (2, or 1 when pairs would leave SMs
+  // idle) consecutive query tiles of one (image, head), `rph` of them per
+  // head.  With pairs and an odd number of query tiles per head, each
+  // head's last tile is paired instead with the next head's last tile
+  // (items from mixed_from on): the two tiles then read different K / V,
+  // but still ping-pong on the tensor core, where a lone tile would run its
+  // chain without a partner.
+  const int nt = (tokens + AQ - 1) / AQ;  // query tiles per head
   const int nb = (tokens + AKV - 1) / AKV;
-  auto item_tiles = [&](int it, int& bh, int& q0) {
-    bh = it / pairs;
-    q0 = (it - bh * pairs) * tpi * AQ;
-    return (tpi == 2 && tokens - q0 > AQ) ? 2 : 1;  // tile 1 may not exist
+  struct Item {
+    int bh[2], q0[2];
+    int ntiles;  // 1 or 2
+    int kvs;     // K / V streams: 2 when the tiles belong to different heads
+  };
+  auto item_of = [&](int it) {
+    Item r;
+    if (it < mixed_from) {
+      const int b = it / rph, p = it - b * rph;
+      r.bh[0] = r.bh[1] = b;
+      r.q0[0] = p * tpi * AQ;
+      r.q0[1] = r.q0[0] + AQ;
+      r.ntiles = (tpi == 2 && tokens - r.q0[0] > AQ) ? 2 : 1;  // tile 1 may not exist
+      r.kvs = 1;
+    } else {
+      const int m = it - mixed_from;
+      r.bh[0] = 2 * m;
+      r.bh[1] = 2 * m + 1;
+      r.q0[0] = r.q0[1] = (nt - 1) * AQ;
+      r.ntiles = r.bh[1] < bh_count ? 2 : 1;
+      r.kvs = r.ntiles;
+    }
+    return r;
   };
 
   if (threadIdx.x == 0) {
@@ -115,25 +142,27 @@ __global__ void __launch_bounds__(A_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      uint32_t g = 0;  // K/V blocks loaded so far
+      uint32_t g = 0;  // K/V stages loaded so far
       bool ok = true;
       for (int it = blockIdx.x, c = 0; it < items && ok; it += gridDim.x, ++c) {
-        int bh, q0;
-        const int ntiles = item_tiles(it, bh, q0);
+        const Item I = item_of(it);
         const int qb = c & 1;
         if (c >= 2 && !mbar_wait(&q_empty[qb], ((c >> 1) - 1) & 1, err, VK_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&q_full[qb], ntiles * TILE_BYTES);
-        for (int t = 0; t < ntiles; ++t)
-          tma_load_3d(sQ + (qb * 2 + t) * TILE_BYTES, &tmQ, &q_full[qb], 0, q0 + t * AQ, bh);
-        for (int j = 0; j < nb; ++j, ++g) {
-          const uint32_t st = g % AST;
-          if (!mbar_wait(&kv_empty[st], ((g / AST) & 1) ^ 1, err, VK_DEV_TIMEOUT_PRODUCER)) {
-            ok = false;
-            break;
+        mbar_arrive_expect_tx(&q_full[qb], I.ntiles * TILE_BYTES);
+        for (int t = 0; t < I.ntiles; ++t)
+          tma_load_3d(sQ + (qb * 2 + t) * TILE_BYTES, &tmQ, &q_full[qb], 0, t ? I.q0[1] : I.q0[0], t ? I.bh[1] : I.bh[0]);
+        // per key block, one stage per K / V stream (in tile order)
+        for (int j = 0; j < nb && ok; ++j) {
+          for (int u = 0; u < I.kvs; ++u, ++g) {
+            const uint32_t st = g % AST;
+            if (!mbar_wait(&kv_empty[st], ((g / AST) & 1) ^ 1, err, VK_DEV_TIMEOUT_PRODUCER)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+            tma_load_3d(sK + st * TILE_BYTES, &tmK, &kv_full[st], 0, j * AKV, u ? I.bh[1] : I.bh[0]);
+            tma_load_3d(sV + st * TILE_BYTES, &tmV, &kv_full[st], 0, j * AKV, u ? I.bh[1] : I.bh[0]);
           }
-          mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
-          tma_load_3d(sK + st * TILE_BYTES, &tmK, &kv_full[st], 0, j * AKV, bh);
-          tma_load_3d(sV + st * TILE_BYTES, &tmV, &kv_full[st], 0, j * AKV, bh);
         }
       }
     }
@@ -149,26 +178,34 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           umma_f16(tmem + t * TILE_COLS + COL_S, qdesc + static_cast<uint64_t>(k * 2),
                    kdesc + static_cast<uint64_t>(k * 2), idS, k > 0 ? 1u : 0u);
       };
-      uint32_t g = 0;                 // K/V blocks consumed so far
+      uint32_t g = 0;                 // K/V stages consumed so far
       uint32_t sp[2] = {0u, 0u};      // per tile: S / P hand-offs so far
       uint32_t ct[2] = {0u, 0u};      // per tile: items so far
       bool ok = true;
+      auto kv_wait = [&](uint32_t gg) {
+        return mbar_wait(&kv_full[gg % AST], (gg / AST) & 1, err, VK_DEV_TIMEOUT_MMA);
+      };
       for (int it = blockIdx.x, c = 0; it < items && ok; it += gridDim.x, ++c) {
-        int bh, q0;
-        const int ntiles = item_tiles(it, bh, q0);
+        const Item I = item_of(it);
+        const int ntiles = I.ntiles;
+        const uint32_t kvs = static_cast<uint32_t>(I.kvs);
         const int qb = c & 1;
         if (!(ok = mbar_wait(&q_full[qb], (c >> 1) & 1, err, VK_DEV_TIMEOUT_MMA))) break;
-        if (!(ok = mbar_wait(&kv_full[g % AST], (g / AST) & 1, err, VK_DEV_TIMEOUT_MMA))) break;
+        for (uint32_t u = 0; u < kvs && ok; ++u) ok = kv_wait(g + u);
+        if (!ok) break;
         tc_fence_after();
+        // stage of tile t's K / V for the block at stage base gb
+        auto st_of = [&](uint32_t gb, int t) { return (gb + (kvs == 2 ? static_cast<uint32_t>(t) : 0u)) % AST; };
         for (int t = 0; t < ntiles; ++t) {  // the previous item's last O_t was issued before
-          issue_s(t, qb, g % AST);
+          issue_s(t, qb, st_of(g, t));
           umma_commit(&s_full[t]);
         }
-        for (int j = 0; j < nb && ok; ++j, ++g) {
+        for (int j = 0; j < nb && ok; ++j, g += kvs) {
           const bool more = j + 1 < nb;
-          if (more && !(ok = mbar_wait(&kv_full[(g + 1) % AST], ((g + 1) / AST) & 1, err, VK_DEV_TIMEOUT_MMA))) break;
-          const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(sV + (g % AST) * TILE_BYTES));
+          if (more && kvs == 1 && !(ok = kv_wait(g + 1))) break;
           for (int t = 0; t < ntiles && ok; ++t) {
+            if (more && kvs == 2 && !(ok = kv_wait(g + 2 + t))) break;
+            const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(sV + st_of(g, t) * TILE_BYTES));
             if (!(ok = mbar_wait(&p_full[t], sp[t] & 1, err, VK_DEV_TIMEOUT_MMA))) break;
             ++sp[t];
             const uint32_t ob = ct[t] & 1;
@@ -189,13 +226,14 @@ __global__ void __launch_bounds__(A_THREADS, 1)
                             vdesc + static_cast<uint64_t>(k * (2048 >> 4)), idO, 1u);
             }
             if (more) {
-              issue_s(t, qb, (g + 1) % AST);
+              issue_s(t, qb, st_of(g + kvs, t));
               umma_commit(&s_full[t]);  // also covers O_t(j)
             } else {
               umma_commit(&o_done[t]);
             }
+            if (kvs == 2) umma_commit(&kv_empty[st_of(g, t)]);  // this tile's stage: S_t(j), O_t(j) issued
           }
-          if (ok) umma_commit(&kv_empty[g % AST]);  // after every MMA that read this stage
+          if (ok && kvs == 1) umma_commit(&kv_empty[g % AST]);  // after every MMA that read this stage
         }
         if (!ok) break;
         umma_commit(&q_empty[qb]);  // every S of this item has been issued
@@ -211,11 +249,12 @@ __global__ void __launch_bounds__(A_THREADS, 1)
     uint32_t sp = 0, ct = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-      int bh, q0;
-      if (t >= item_tiles(it, bh, q0)) continue;
+      const Item I = item_of(it);
+      if (t >= I.ntiles) continue;
+      const int bh = t ? I.bh[1] : I.bh[0], q0 = t ? I.q0[1] : I.q0[0];
       if (it + static_cast<int>(gridDim.x) >= items && items <= VK_EARLY_LAUNCH_ROUNDS * static_cast<int>(gridDim.x))
         grid_launch_dependents();
-      const int qrow = q0 + t * AQ + quad * 32 + lane;
+      const int qrow = q0 + quad * 32 + lane;
       const uint32_t col_o = COL_O + (ct & 1) * 64;
       float m_ref = -INFINITY;
       float l_run = 0.0f;
@@ -479,10 +518,27 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
                                int heads, int tokens, void* out, __half* q8d, int* err, cudaStream_t s) {
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(k_attention_tc<OUT, SPLIT>), static_cast<int>(ATT_SMEM));
   if (e != cudaSuccess) return e;
-  // tile pairs share each K/V block; single tiles when pairs would not fill the SMs
+  // tile pairs share each K/V block; single tiles when pairs would not fill
+  // the SMs.  With pairs and an odd tile count per head, the heads' last
+  // tiles pair up across heads (items from mixed_from on).
+  const int bh_count = images * heads;
+  const int nt = (tokens + AQ - 1) / AQ;
   int tpi = 2;
-  if (((tokens + 2 * AQ - 1) / (2 * AQ)) * images * heads < num_sms()) tpi = 1;
-  const int items = ((tokens + tpi * AQ - 1) / (tpi * AQ)) * images * heads;
+  if (((tokens + 2 * AQ - 1) / (2 * AQ)) * bh_count < num_sms()) tpi = 1;
+  static const bool no_mix = getenv("VK_ATT_NO_MIX") != nullptr;
+  int rph, mixed_from, items;
+  if (tpi == 1) {
+    rph = nt;
+    items = mixed_from = nt * bh_count;
+  } else if (no_mix || nt % 2 == 0) {
+    // (VK_ATT_NO_MIX: a head's odd last tile runs alone, as its own item)
+    rph = (nt + 1) / 2;
+    items = mixed_from = rph * bh_count;
+  } else {
+    rph = nt / 2;
+    mixed_from = rph * bh_count;
+    items = mixed_from + (bh_count + 1) / 2;
+  }
   const int grid = items < num_sms() ? items : num_sms();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -494,7 +550,8 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
   la[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = la;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_attention_tc<OUT, SPLIT>, mq, mk, mv, heads, tokens, items, tpi, out, q8d, err);
+  return cudaLaunchKernelEx(&cfg, k_attention_tc<OUT, SPLIT>, mq, mk, mv, heads, tokens, items, tpi, rph, mixed_from,
+                            bh_count, out, q8d, err);
 }
 
 cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* v, int images,
