@@ -257,12 +257,14 @@ def test_flash_attention_f32(vk, ctx, oracle_lib, tokens):
     assert d.mean() <= 5e-5 and d.max() <= 5e-4  # src/cuda.rs:1613-1648 bounds
 
 
-@pytest.mark.parametrize("tokens,heads", [(865, 12), (865, 48), (865, 75), (300, 101), (3457, 2), (64, 3), (65, 1), (1, 2),
-                                           (97, 301)])
+@pytest.mark.parametrize("tokens,heads", [(865, 12), (865, 48), (865, 75), (300, 101), (1000, 40), (3457, 2), (64, 3),
+                                           (65, 1), (1, 2), (97, 301)])
 def test_flash_attention_bf16(vk, ctx, oracle_lib, tokens, heads):
     """(865, 48), (865, 75), (300, 101), (97, 301): enough heads for tile
     pairs with an odd tile count per head, so the heads' last tiles pair up
-    across heads (75, 101, 301: one left alone)."""
+    across heads (75, 101, 301: one left alone).  (865, 48) and (1000, 40):
+    168 and 160 items on 148 CTAs, so the last round's items run as single
+    tiles."""
     ctx.set_math(vk.MATH_BF16)
     try:
         q, k, v = (oracle_lib.round_bf16(t) for t in rng_inputs(80 + tokens, *[(heads, tokens, 64)] * 3))

@@ -63,7 +63,7 @@ template <int OUT, bool SPLIT>
 __global__ void __launch_bounds__(A_THREADS, 1)
     k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, int heads, int tokens, int items, int tpi, int rph,
-                   int mixed_from, int bh_count, void* out, __half* out_q8d, int* err) {
+                   int mixed_from, int bh_count, int split_from, void* out, __half* out_q8d, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;  // [item parity][tile]
@@ -95,7 +95,10 @@ __global__ void __launch_bounds__(A_THREADS, 1)
     int ntiles;  // 1 or 2
     int kvs;     // K / V streams: 2 when the tiles belong to different heads
   };
-  auto item_of = [&](int it) {
+  // Items from split_from on are the tiles of the last round's two-tile
+  // items taken one by one (2 per such item), so that a last round that
+  // would leave most CTAs idle is spread over twice as many CTAs.
+  auto pair_of = [&](int it) {
     Item r;
     if (it < mixed_from) {
       const int b = it / rph, p = it - b * rph;
@@ -112,6 +115,18 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       r.ntiles = r.bh[1] < bh_count ? 2 : 1;
       r.kvs = r.ntiles;
     }
+    return r;
+  };
+  auto item_of = [&](int it) {
+    if (it < split_from) return pair_of(it);
+    const int u = it - split_from;
+    Item r = pair_of(split_from + (u >> 1));  // a two-tile item (the host checks)
+    if (u & 1) {
+      r.bh[0] = r.bh[1];
+      r.q0[0] = r.q0[1];
+    }
+    r.ntiles = 1;
+    r.kvs = 1;
     return r;
   };
 
@@ -539,6 +554,21 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
     mixed_from = rph * bh_count;
     items = mixed_from + (bh_count + 1) / 2;
   }
+  // A last round of r two-tile items on the persistent grid leaves the other
+  // CTAs idle while it runs; when 2 r single tiles fit in one round, run the
+  // r items as single tiles instead (a lone tile takes about 0.87 of a pair's
+  // time).  Every item in that range must hold two tiles.
+  int split_from = items;
+  static const bool no_split = getenv("VK_ATT_NO_SPLIT_TAIL") != nullptr;
+  const int g0 = num_sms();
+  const int r = items % g0;
+  // every item holds two tiles: cross-head items pair all heads (an even
+  // count), and otherwise each head's last pair has its second tile
+  const bool last_pairs = tpi == 2 && (items == mixed_from ? (tokens - (rph - 1) * 2 * AQ > AQ) : (bh_count % 2 == 0));
+  if (!no_split && items > g0 && r > 0 && 2 * r <= g0 && last_pairs) {
+    split_from = items - r;
+    items += r;
+  }
   const int grid = items < num_sms() ? items : num_sms();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -551,7 +581,7 @@ static cudaError_t launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, con
   cfg.attrs = la;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k_attention_tc<OUT, SPLIT>, mq, mk, mv, heads, tokens, items, tpi, rph, mixed_from,
-                            bh_count, out, q8d, err);
+                            bh_count, split_from, out, q8d, err);
 }
 
 cudaError_t attention_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* v, int images,
