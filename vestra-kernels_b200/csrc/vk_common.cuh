@@ -60,11 +60,13 @@ __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepco
 // starts its last unit of work, and only for small grids (a few rounds of
 // work per CTA, as with 8 images per GPU), so that the next kernel's CTAs
 // take the SMs of CTAs that finish early.  Measured on the 12-layer
-// forward: +2.2% at 8 images, -1.8% at 64 (where it is not issued).  Every
+// forward: +2.2% at 8 images with a 4-round limit, a further +0.5% with 8
+// rounds (fc1's 5 rounds at 8 images), -1.8% at 64 if issued there (where
+// the grids have 9 or more rounds and it is not).  Every
 // CTA of this grid is resident by the time the dependents launch, so they
 // cannot starve it; their griddepcontrol.wait still waits for this grid to
 // complete.
-constexpr int VK_EARLY_LAUNCH_ROUNDS = 4;
+constexpr int VK_EARLY_LAUNCH_ROUNDS = 8;
 __device__ __forceinline__ void grid_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
